@@ -1,0 +1,366 @@
+"""Benchmark: fused causal top-K retrieval + sparse attention forward on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl wayfinder|reference] [--config cfg2]
+
+One rank per GPU (torchrun for N > 1).  Each rank runs its own batch element of
+the workload (batch sharding, no collective on the data path: weak scaling).
+Prints ONE JSON line on rank 0.
+
+Timing: W untimed warm-up steps, then exactly K steps between a barrier +
+cuda.synchronize() on both sides.  Before every timed step a 256 MiB memset
+(2x the 126 MB L2) flushes the cache; each step is bracketed by CUDA events on
+the launching stream, so the flush is outside the timed region.  The per-rank
+time is the sum of step times; the job time is the max over ranks.
+
+``value`` is queries/s (token positions B*T per step, all ranks) with inputs
+resident in HBM; ``e2e`` is the same metric through the public API with the
+inputs copied from pinned host memory and the outputs read back every step.
+``--impl reference`` times the CPU oracle port of the reference path on the
+host cores instead (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+from wayfinder_attention_b200.workloads import CONFIGS, Workload, make_inputs, scaled, to_device  # noqa: E402
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 256 << 20
+METRIC = "fused top-K+sparse-attn fwd queries/s @T=16K,K=128"
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def dist_env() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+class ClockSampler:
+    """nvidia-smi sampler run during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_model() -> str:
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_sample_rows(T: int, n: int) -> np.ndarray:
+    """Evenly spread query rows: their mean causal length is T/2, like the full job."""
+    return np.unique(np.linspace(0, T - 1, n).astype(np.int64))
+
+
+def time_cpu_oracle(w: Workload, inputs: dict, n_rows: int) -> tuple[float, int]:
+    """Seconds for the oracle port on ``n_rows`` sampled rows of batch element 0 (all host threads)."""
+    from oracle import wayfinder_oracle as oracle  # CPU baseline leg only
+
+    xn = {k: v[:1].float().contiguous().numpy() for k, v in inputs.items()}
+    rows = cpu_sample_rows(w.T, n_rows)
+    t0 = time.perf_counter()
+    oracle.fused_sparse_attention(xn["q_addr"], xn["k_addr"], xn["q"], xn["k"], xn["v"], w.K, w.D ** -0.5,
+                                  rows=rows)
+    return time.perf_counter() - t0, rows.size
+
+
+def run_reference_arm(args, w: Workload) -> None:
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    inputs = make_inputs(w, B=1)
+    n_rows = args.cpu_rows
+    for _ in range(max(args.warmup, 0)):
+        time_cpu_oracle(w, inputs, min(n_rows, 64))
+    secs = []
+    for _ in range(args.steps):
+        s, n = time_cpu_oracle(w, inputs, n_rows)
+        secs.append(s)
+    total = sum(secs)
+    value = n * args.steps / total
+    line = {
+        "impl": "reference",
+        "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seed 45)",
+        "config": {"workload": w.name, "B": 1, "H": w.H, "T": w.T, "D": w.D, "d_A": w.R, "K": w.K,
+                   "sample_rows_per_step": n},
+        "cpu_baseline": {"value": value, "unit": "queries/s", "cores": threads, "kind": "port",
+                         "cpu": cpu_model(),
+                         "sample": f"{n} evenly spaced query rows of one T={w.T} sequence per step "
+                                   f"(retrieval over their causal prefixes + attention over {w.H} heads)"},
+        "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="wayfinder", choices=["wayfinder", "reference"])
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--cpu-rows", type=int, default=1024, help="rows per reference-arm step")
+    ap.add_argument("--cpu-baseline-rows", type=int, default=16384, help="rows of the one-off cpu_baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-dense", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    w = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference_arm(args, w)
+        return
+
+    import torch.distributed as dist
+
+    from wayfinder_attention_b200 import _lib
+    from wayfinder_attention_b200.causal_topk import _launch_topk
+    from wayfinder_attention_b200.fused_sparse import _launch_attention, fused_sparse_attention
+
+    rank, local_rank, world = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # batch sharding: each rank owns batch element(s) `rank` of a global batch of world * B
+    w_local = scaled(w, B=w.B)
+    host = make_inputs(w_local, batch_offset=rank)
+    x = to_device(host, dev)
+    K = w.K
+    scale = w.D ** -0.5
+    idx = torch.empty(w.B, w.T, min(K, w.T), dtype=torch.int32, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        _launch_topk(x["q_addr"], x["k_addr"], K, "reference", out=idx)
+        return _launch_attention(x["q"], x["k"], x["v"], idx, scale, mask_negative=False, out_dtype=None)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    torch.cuda.reset_peak_memory_stats(dev)
+    mem0 = torch.cuda.memory_allocated(dev)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            _launch_topk(x["q_addr"], x["k_addr"], K, "reference", out=idx)
+            ev[i][1].record(stream)
+            _launch_attention(x["q"], x["k"], x["v"], idx, scale, mask_negative=False, out_dtype=None)
+            ev[i][2].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    peak_mb = (torch.cuda.max_memory_allocated(dev) - mem0) / 2**20
+    topk_ms = [e[0].elapsed_time(e[1]) for e in ev]
+    attn_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    total_ms = sum(topk_ms) + sum(attn_ms)
+    t = torch.tensor([total_ms, sum(topk_ms), sum(attn_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, topk_tot, attn_tot = t.tolist()
+    ms_per_step = total_ms / args.steps
+    queries = w.B * w.T * world
+    value = queries / (ms_per_step / 1e3)
+
+    # end-to-end through the public API: pinned host inputs -> device -> op -> host outputs
+    pin = {k: (v.transpose(1, 2).contiguous() if v.dim() == 4 else v.contiguous()).pin_memory()
+           for k, v in host.items()}
+    dbuf = {k: torch.empty_like(v, device=dev) for k, v in pin.items()}
+    out_h = torch.empty(w.B, w.H, w.T, w.D, dtype=w.dtype).pin_memory()
+    idx_h = torch.empty(w.B, w.T, min(K, w.T), dtype=torch.int32).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in pin.values())
+    d2h = out_h.numel() * out_h.element_size() + idx_h.numel() * idx_h.element_size()
+
+    def e2e_step():
+        for k_ in pin:
+            dbuf[k_].copy_(pin[k_], non_blocking=True)
+        q, k, v = (dbuf[n].transpose(1, 2) for n in ("q", "k", "v"))
+        out, ii = fused_sparse_attention(dbuf["q_addr"], dbuf["k_addr"], q, k, v, K, scale)
+        out_h.copy_(out, non_blocking=True)
+        idx_h.copy_(ii, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    e_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()
+        e_ev[i][0].record(stream)
+        e2e_step()
+        e_ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = torch.tensor([sum(a.elapsed_time(b) for a, b in e_ev)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = queries / (e2e_ms.item() / args.steps / 1e3)
+
+    result = None
+    if rank == 0:
+        peaks, peak_kind = load_peaks()
+        attn_ms_launch = attn_tot / args.steps
+        topk_ms_launch = topk_tot / args.steps
+        gathered = w.gathered_bytes()
+        achieved_gbs = gathered / (attn_ms_launch / 1e3) / 1e9
+        hbm = float(peaks["hbm_gbs"])
+        tens = float(peaks["bf16_tflops"]) * 1e12
+        roof_s = max(w.score_flops() / tens, gathered / (hbm * 1e9))
+        result = {
+            "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if w.dtype == torch.bfloat16 else str(w.dtype).split(".")[-1],
+            "data": "synthetic (seeded N(0,1) q/k/v, N(0,1/32) addresses)",
+            "config": {"workload": w.name, "B": w.B, "H": w.H, "T": w.T, "D": w.D, "d_A": w.R, "K": K,
+                       "global_batch": w.B * world, "seq_len": w.T,
+                       "parallelism": f"batch-sharded x{world} (no collective)",
+                       "l2": "flushed before every timed step (256 MiB memset, outside the events)"},
+            "latency_ms": ms_per_step,
+            "query_heads_per_s": value * w.H,
+            "kernels_ms": {"causal_topk": topk_ms_launch, "sparse_attention": attn_ms_launch},
+            "roofline": {"kernel": "sparse_attention", "bound": "hbm", "achieved": achieved_gbs, "peak": hbm,
+                         "unit": "GB/s", "frac": achieved_gbs / hbm, "traffic": None,
+                         "peak_kind": peak_kind,
+                         "note": "achieved = gathered K/V bytes (2*B*H*T*K*D*2) / kernel time; K/V fit in L2"},
+            "path_roofline": {"roofline_ms": roof_s * 1e3, "frac": roof_s * 1e3 / ms_per_step,
+                              "score_tflops_achieved": w.score_flops() / (topk_ms_launch / 1e3) / 1e12,
+                              "definition": "max(score FLOPs / bf16 peak, gathered bytes / HBM peak) / latency"},
+            "peak_mb": peak_mb,
+            "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms.item() / args.steps},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }
+        if not args.no_dense:
+            result["dense_sdpa"] = dense_baseline(w, x, flush, args.steps)
+        if world == 1 and not args.no_cpu_baseline:
+            secs, n = time_cpu_oracle(w, host, args.cpu_baseline_rows)
+            result["cpu_baseline"] = {
+                "value": n / secs, "unit": "queries/s", "cores": os.cpu_count() or 1, "kind": "port",
+                "cpu": cpu_model(),
+                "sample": f"{n} evenly spaced query rows of the T={w.T} sequence "
+                          f"(retrieval + {w.H}-head attention), numpy fp32 oracle",
+            }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+def dense_baseline(w: Workload, x: dict, flush: torch.Tensor, steps: int) -> dict:
+    """Dense causal SDPA at the same shape (the reference's DenseSDPAAttention call), for comparison."""
+    import torch.nn.functional as F
+
+    dev = x["q"].device
+    q, k, v = x["q"], x["k"], x["v"]
+    for _ in range(3):
+        F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=w.D ** -0.5)
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats(dev)
+    m0 = torch.cuda.memory_allocated(dev)
+    tot = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=w.D ** -0.5)
+        b.record()
+        torch.cuda.synchronize()
+        tot += a.elapsed_time(b)
+    return {"ms": tot / steps, "peak_mb": (torch.cuda.max_memory_allocated(dev) - m0) / 2**20,
+            "queries_per_s": w.B * w.T / (tot / steps / 1e3)}
+
+
+if __name__ == "__main__":
+    main()

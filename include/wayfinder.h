@@ -1,0 +1,125 @@
+/*
+ * wayfinder.h — C ABI of libwayfinder_sm100.so, the B200 (sm_100a) kernels for
+ * Wayfinder's causal learned-address retrieval + sparse attention forward.
+ *
+ * Every entry point takes plain device pointers, sizes and element strides,
+ * enqueues work on the given CUDA stream and returns without synchronising.
+ * Return value: WF_OK (0) or an error code; wf_last_error() then holds a
+ * message for the calling thread.  Inputs are never written.
+ *
+ * Reference interfaces replaced (paths inside Wayland-The-Smith/wayfinder-attention):
+ *   wf_causal_topk            <- routing_attention/kernels/causal_topk.py:470-521   causal_topk()
+ *   wf_sparse_attention       <- routing_attention/kernels/fused_sparse.py:275-324  sparse_meat_attention()
+ *   wf_fused_sparse_attention <- routing_attention/kernels/fused_sparse.py:327-356  fused_sparse_attention()
+ */
+#ifndef WAYFINDER_H_
+#define WAYFINDER_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define WF_API __attribute__((visibility("default")))
+#else
+#define WF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types. */
+#define WF_DTYPE_BF16 0
+#define WF_DTYPE_F16 1
+#define WF_DTYPE_F32 2
+
+/* Return codes. */
+#define WF_OK 0
+#define WF_ERR_INVALID_ARGUMENT 1 /* bad shape, stride, pointer or value (Python: ValueError)   */
+#define WF_ERR_UNSUPPORTED 2      /* valid request this build does not cover (Python: ValueError) */
+#define WF_ERR_CUDA 3             /* CUDA launch/runtime failure (Python: RuntimeError)          */
+
+/* Pad policy for query rows that have fewer than K causal keys (rows i < K-1). */
+#define WF_PAD_REFERENCE 0 /* slot s >= i+1 gets index (i + K + s + 1) % T, attended unmasked,
+                              as routing_attention/kernels/causal_topk.py:37-57 does        */
+#define WF_PAD_MASKED 1    /* slot s >= i+1 gets -1 and is excluded from the softmax        */
+
+/* Attention flags. */
+#define WF_ATTN_MASK_NEGATIVE 1 /* a negative index is a masked slot (otherwise it wraps by T,
+                                   like torch advanced indexing)                              */
+
+/* Library version (major * 100 + minor). */
+WF_API int wf_version(void);
+
+/* Message describing the last error returned on this thread ("" if none). */
+WF_API const char* wf_last_error(void);
+
+/* Largest top_k that wf_causal_topk / wf_fused_sparse_attention accept. */
+WF_API int wf_max_top_k(void);
+
+/*
+ * Exact causal top-K inner-product retrieval.  Replaces causal_topk()
+ * (routing_attention/kernels/causal_topk.py:470-521; default path
+ * _causal_topk_row_blocked :133-171 + _finalize_causal_topk :37-57).
+ *
+ *   q_addr  : (B, Tq, R) query addresses, strides q_strides[3] in elements
+ *   k_addr  : (B, Tk, R) key addresses,   strides k_strides[3] in elements
+ *   dtype   : WF_DTYPE_* of both address tensors (scores are computed in fp32)
+ *   top_k   : requested K; K_eff = min(top_k, Tk) slots are written per row
+ *   pad_mode: WF_PAD_REFERENCE or WF_PAD_MASKED
+ *   row map : local query row l sits at sequence position
+ *             g(l) = ((l / row_tile) * row_stride + row_start) * row_tile + l % row_tile
+ *             and may retrieve keys j <= g(l).  row_tile = 0 selects the identity map
+ *             (g(l) = l).  Otherwise row_tile must be a multiple of 64, row_stride >= 1,
+ *             0 <= row_start < row_stride, and every g(l) < Tk.  This is how a rank of a
+ *             query-row-sharded long sequence addresses its cyclic row blocks.
+ *   idx_out : (B, Tq, K_eff) int32, contiguous.  Slots hold the retrieved key indices in
+ *             descending score order; equal scores break to the lower index.
+ */
+WF_API int wf_causal_topk(const void* q_addr, const void* k_addr, int32_t dtype, int64_t B, int64_t Tq,
+                   int64_t Tk, int32_t R, const int64_t* q_strides, const int64_t* k_strides,
+                   int32_t top_k, int32_t pad_mode, int32_t row_tile, int32_t row_stride,
+                   int32_t row_start, int32_t* idx_out, void* stream);
+
+/*
+ * Softmax attention over the K rows named by idx, shared by all heads.  Replaces
+ * sparse_meat_attention() (routing_attention/kernels/fused_sparse.py:275-324; the
+ * arithmetic of sparse_meat_attention_reference :80-94), computed in fp32.
+ *
+ *   q        : (B, H, Tq, D)      strides q_strides[4]   (last stride must be 1)
+ *   k, v     : (B, H, Tk, D)      strides k_strides[4], v_strides[4] (last stride 1)
+ *   dtype    : WF_DTYPE_* of q, k and v
+ *   idx      : (B, Tq, K) int32   strides idx_strides[3]
+ *   D        : 16, 32, 64, 128 or 256; rows must start on 16-byte boundaries
+ *   flags    : WF_ATTN_MASK_NEGATIVE or 0
+ *   out      : (B, H, Tq, D) of out_dtype, strides out_strides[4] (last stride 1)
+ *   status   : optional device int32; bit 0 is OR-ed in when an index lies outside
+ *              [-Tk, Tk) (that row's output is NaN).  May be NULL.
+ */
+WF_API int wf_sparse_attention(const void* q, const void* k, const void* v, int32_t dtype,
+                        const int32_t* idx, int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t D,
+                        int32_t K, const int64_t* q_strides, const int64_t* k_strides,
+                        const int64_t* v_strides, const int64_t* idx_strides, float scale,
+                        int32_t flags, void* out, int32_t out_dtype, const int64_t* out_strides,
+                        int32_t* status, void* stream);
+
+/*
+ * Retrieval + attention in one call.  Replaces fused_sparse_attention()
+ * (routing_attention/kernels/fused_sparse.py:327-356): wf_causal_topk into idx_out,
+ * then wf_sparse_attention over it (masking pads when pad_mode == WF_PAD_MASKED).
+ * Arguments have the meanings given above; addr_dtype may differ from dtype.
+ */
+WF_API int wf_fused_sparse_attention(const void* q_addr, const void* k_addr, int32_t addr_dtype, int32_t R,
+                              const int64_t* q_addr_strides, const int64_t* k_addr_strides,
+                              const void* q, const void* k, const void* v, int32_t dtype, int64_t B,
+                              int64_t H, int64_t Tq, int64_t Tk, int32_t D,
+                              const int64_t* q_strides, const int64_t* k_strides,
+                              const int64_t* v_strides, int32_t top_k, float scale,
+                              int32_t pad_mode, int32_t row_tile, int32_t row_stride,
+                              int32_t row_start, int32_t* idx_out, void* out, int32_t out_dtype,
+                              const int64_t* out_strides, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WAYFINDER_H_ */

@@ -1,0 +1,44 @@
+"""Wayfinder causal learned-address retrieval + sparse attention on B200 (sm_100a).
+
+Public API (names and arguments of the reference's ``routing_attention``):
+  causal_topk, fused_sparse_attention, sparse_meat_attention, SparseMeatConfig,
+  LearnedAddressSparseAttention, LearnedAddressModule, RetrievalConfig,
+  TransformerLM (the decoder harness).
+
+The compute runs in ``libwayfinder_sm100.so`` (C ABI: ``include/wayfinder.h``);
+there is no CPU path.
+"""
+
+from ._lib import load_library
+from .attention import (
+    LearnedAddressModule,
+    LearnedAddressSparseAttention,
+    RetrievalConfig,
+    retrieval_config_from_dict,
+)
+from .causal_topk import causal_topk, causal_topk_available, promote_compute_dtype
+from .decoder import DenseSDPAAttention, TransformerBlock, TransformerLM
+from .fused_sparse import (
+    SparseMeatConfig,
+    fused_sparse_attention,
+    fused_sparse_attention_available,
+    sparse_meat_attention,
+)
+
+__all__ = [
+    "load_library",
+    "causal_topk",
+    "causal_topk_available",
+    "promote_compute_dtype",
+    "fused_sparse_attention",
+    "fused_sparse_attention_available",
+    "sparse_meat_attention",
+    "SparseMeatConfig",
+    "LearnedAddressModule",
+    "LearnedAddressSparseAttention",
+    "RetrievalConfig",
+    "retrieval_config_from_dict",
+    "DenseSDPAAttention",
+    "TransformerBlock",
+    "TransformerLM",
+]

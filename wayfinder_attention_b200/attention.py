@@ -1,0 +1,183 @@
+"""``LearnedAddressSparseAttention`` on the sm_100a kernels.
+
+Drop-in for the reference module of the same name
+(``routing_attention/models/attention.py:409-501``) and its address module
+(``routing_attention/models/learned_address.py:12-56``): same constructor
+signature, same submodule names (``q_proj``, ``k_proj``, ``v_proj``,
+``out_proj``, ``address.q_addr_proj``, ``address.k_addr_proj``), so reference
+``state_dict``s load unchanged.  Projections, address normalisation and
+``out_proj`` stay in PyTorch; retrieval + sparse attention run in the CUDA
+library.
+
+Differences from the reference module, all deliberate:
+  * no ``RoutingRetriever`` is built, so no ``max_seq_len**2`` causal mask is
+    allocated (``retrieval/index.py:112-113``);
+  * both module paths call the same exact kernel.  With
+    ``use_fused_sparse=False`` the addresses are first rounded to
+    ``retrieval_config.dtype`` (fp16 by default), reproducing the non-fused
+    path's retrieval numerics (``retrieval/index.py:188-207``);
+  * the sparse attention is forward-only (the reference's fused path is
+    ``@torch.no_grad`` too, ``kernels/fused_sparse.py:327``).  Attention-
+    probability dropout of the non-fused path is not implemented: calling it
+    in training mode with ``dropout > 0`` raises ``NotImplementedError``.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, fields
+from typing import Literal, Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .causal_topk import causal_topk
+from .fused_sparse import fused_sparse_attention, sparse_meat_attention
+
+
+@dataclass
+class RetrievalConfig:
+    """Fields of ``routing_attention/retrieval/index.py:82-98``; only
+    ``top_k``, ``use_fused_sparse`` and ``dtype`` influence this build."""
+
+    method: str = "auto"
+    top_k: int = 32
+    max_seq_len: int = 8192
+    oversample: int = 4
+    dtype: Literal["float32", "float16", "bfloat16"] = "float16"
+    brute_force_max_seq: int = 2048
+    faiss_flat_max_seq: int = 16384
+    hnsw_m: int = 32
+    hnsw_ef_search: int = 64
+    use_gpu: bool = True
+    apply_to_key_vector: bool = False
+    use_fused_sparse: bool = False
+
+
+def retrieval_config_from_dict(d: dict | None) -> RetrievalConfig:
+    """Like ``retrieval/index.py:372-387``: unknown keys are ignored."""
+    d = d or {}
+    names = {f.name for f in fields(RetrievalConfig)}
+    return RetrievalConfig(**{k: v for k, v in d.items() if k in names})
+
+
+def _resolve_retrieval_cfg(cfg: RetrievalConfig | dict | None, top_k: int) -> RetrievalConfig:
+    if isinstance(cfg, dict):
+        return retrieval_config_from_dict(cfg)
+    return cfg or RetrievalConfig(top_k=top_k)
+
+
+class LearnedAddressModule(nn.Module):
+    """Query/key address projections + L2 normalisation (``learned_address.py:12-56``)."""
+
+    def __init__(
+        self,
+        d_model: int,
+        address_dim: int = 32,
+        similarity: Literal["symmetric", "asymmetric"] = "asymmetric",
+        normalize: bool = True,
+    ):
+        super().__init__()
+        self.d_model = d_model
+        self.address_dim = address_dim
+        self.similarity = similarity
+        self.normalize = normalize
+        self.q_addr_proj = nn.Linear(d_model, address_dim)
+        self.k_addr_proj = nn.Linear(d_model, address_dim) if similarity == "asymmetric" else None
+
+    def forward_query_key(self, hidden: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        q = self.q_addr_proj(hidden)
+        k = self.k_addr_proj(hidden) if self.k_addr_proj is not None else q
+        if self.normalize:
+            q = F.normalize(q, dim=-1)
+            k = F.normalize(k, dim=-1)
+        return q, k
+
+    def forward(self, hidden: torch.Tensor) -> torch.Tensor:
+        q, _ = self.forward_query_key(hidden)
+        return q
+
+    def retrieval_scores(self, hidden: torch.Tensor) -> torch.Tensor:
+        q, k = self.forward_query_key(hidden)
+        return torch.matmul(q, k.transpose(-2, -1))
+
+
+_DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32}
+
+
+class LearnedAddressSparseAttention(nn.Module):
+    """Learned addresses pick K causal candidates; softmax attention runs on that subset."""
+
+    def __init__(
+        self,
+        d_model: int,
+        n_heads: int,
+        top_k: int = 32,
+        address_dim: int = 32,
+        similarity: Literal["symmetric", "asymmetric"] = "asymmetric",
+        dropout: float = 0.1,
+        address_module: LearnedAddressModule | None = None,
+        retrieval_config: RetrievalConfig | dict | None = None,
+        pad_mode: str = "reference",
+    ):
+        super().__init__()
+        assert d_model % n_heads == 0
+        self.n_heads = n_heads
+        self.head_dim = d_model // n_heads
+        self.scale = self.head_dim ** -0.5
+        self.top_k = top_k
+        self.pad_mode = pad_mode
+        self._retrieval_cfg = _resolve_retrieval_cfg(retrieval_config, top_k)
+        self.q_proj = nn.Linear(d_model, d_model)
+        self.k_proj = nn.Linear(d_model, d_model)
+        self.v_proj = nn.Linear(d_model, d_model)
+        self.out_proj = nn.Linear(d_model, d_model)
+        self.dropout = nn.Dropout(dropout)
+        self.address = address_module or LearnedAddressModule(
+            d_model=d_model, address_dim=address_dim, similarity=similarity
+        )
+
+    def set_address_module(self, address_module: LearnedAddressModule) -> None:
+        self.address = address_module
+
+    def forward(
+        self,
+        x: torch.Tensor,
+        attn_mask: Optional[torch.Tensor] = None,
+        return_attention: bool = False,
+        **kwargs,
+    ):
+        # attn_mask is accepted and ignored, as on the reference's sparse path (attention.py:456-490).
+        B, T, D = x.shape
+        q = self.q_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
+        k = self.k_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
+        v = self.v_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
+        q_addr, k_addr = self.address.forward_query_key(x)
+        if self._retrieval_cfg.use_fused_sparse:
+            meat, candidate_idx = fused_sparse_attention(
+                q_addr, k_addr, q, k, v, self.top_k, self.scale, pad_mode=self.pad_mode
+            )
+        else:
+            if self.training and self.dropout.p > 0:
+                raise NotImplementedError(
+                    "attention-probability dropout of the non-fused path is not implemented "
+                    "(forward-only kernels); use eval() or retrieval_config.use_fused_sparse=True"
+                )
+            rdt = _DTYPES.get(self._retrieval_cfg.dtype, torch.float16)
+            candidate_idx = causal_topk(q_addr.to(rdt), k_addr.to(rdt), self.top_k, pad_mode=self.pad_mode)
+            meat = sparse_meat_attention(
+                q, k, v, candidate_idx, self.scale, mask_negative=self.pad_mode == "masked"
+            )
+        out = meat.transpose(1, 2).contiguous().view(B, T, D)
+        out = self.out_proj(out)
+        if return_attention:
+            # Same debug map as attention.py:492-500 (1/K at each retrieved position), built vectorised.
+            k_eff = candidate_idx.shape[-1]
+            attn_dense = torch.zeros(B, T, T, device=x.device)
+            if k_eff > 0:
+                idx = candidate_idx.long()
+                # masked pad slots (-1) are redirected to slot 0, which always holds a real key
+                idx = torch.where(idx >= 0, idx, idx[..., :1])
+                attn_dense.scatter_(2, idx, 1.0 / k_eff)
+            return out, attn_dense
+        return out

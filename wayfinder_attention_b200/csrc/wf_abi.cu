@@ -1,0 +1,210 @@
+// C ABI of libwayfinder_sm100.so: argument validation, error reporting and
+// dispatch to the kernels.  See include/wayfinder.h for the contract.
+#include "../../include/wayfinder.h"
+#include "wf_kernels.h"
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int ok() {
+  g_err.clear();
+  return WF_OK;
+}
+
+int cuda_fail(int rc, const char* what) {
+  if (rc < 0) return fail(WF_ERR_UNSUPPORTED, "%s: unsupported configuration", what);
+  return fail(WF_ERR_CUDA, "%s: CUDA error %d (%s)", what, rc, cudaGetErrorString((cudaError_t)rc));
+}
+
+bool valid_dtype(int32_t d) { return d == WF_DTYPE_BF16 || d == WF_DTYPE_F16 || d == WF_DTYPE_F32; }
+int dtype_size(int32_t d) { return d == WF_DTYPE_F32 ? 4 : 2; }
+
+constexpr int64_t kI32Max = 2147483647;
+
+int check_topk(const void* q_addr, const void* k_addr, int32_t dtype, int64_t B, int64_t Tq,
+               int64_t Tk, int32_t R, const int64_t* qs, const int64_t* ks, int32_t top_k,
+               int32_t pad_mode, int32_t& rt, int32_t& rs, int32_t& r0, const int32_t* idx_out,
+               int32_t* k_eff_out) {
+  if (B < 0 || Tq < 0 || Tk < 0) return fail(WF_ERR_INVALID_ARGUMENT, "negative size (B=%lld, Tq=%lld, Tk=%lld)",
+                                             (long long)B, (long long)Tq, (long long)Tk);
+  if (R < 1) return fail(WF_ERR_INVALID_ARGUMENT, "address dim R must be >= 1, got %d", R);
+  if (top_k < 0) return fail(WF_ERR_INVALID_ARGUMENT, "top_k must be >= 0, got %d", top_k);
+  if (!valid_dtype(dtype)) return fail(WF_ERR_INVALID_ARGUMENT, "unknown address dtype %d", dtype);
+  if (pad_mode != WF_PAD_REFERENCE && pad_mode != WF_PAD_MASKED)
+    return fail(WF_ERR_INVALID_ARGUMENT, "unknown pad_mode %d", pad_mode);
+  if (Tk > kI32Max || Tq > kI32Max || B > 65535)
+    return fail(WF_ERR_UNSUPPORTED, "sizes too large (B <= 65535 and T < 2^31 required)");
+  const int64_t k_eff = top_k < Tk ? top_k : Tk;
+  *k_eff_out = (int32_t)k_eff;
+  if (k_eff == 0 || B == 0 || Tq == 0) return ok();
+  if (!q_addr || !k_addr || !idx_out || !qs || !ks) return fail(WF_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (k_eff > wf::topk_max_k())
+    return fail(WF_ERR_UNSUPPORTED, "top_k=%lld exceeds this build's maximum of %d", (long long)k_eff,
+                wf::topk_max_k());
+  if (wf::topk_smem_bytes(R, (int)k_eff) == 0)
+    return fail(WF_ERR_UNSUPPORTED, "address dim R=%d with top_k=%lld exceeds shared memory", R, (long long)k_eff);
+  if (rt == 0) {
+    rt = (int32_t)(((Tq + 63) / 64) * 64);
+    rs = 1;
+    r0 = 0;
+  } else {
+    if (rt < 0 || rt % 64 != 0) return fail(WF_ERR_INVALID_ARGUMENT, "row_tile must be a positive multiple of 64, got %d", rt);
+    if (rs < 1 || r0 < 0 || r0 >= rs)
+      return fail(WF_ERR_INVALID_ARGUMENT, "need row_stride >= 1 and 0 <= row_start < row_stride (got %d, %d)", rs, r0);
+  }
+  const int64_t l = Tq - 1;
+  const int64_t gmax = ((l / rt) * rs + r0) * (int64_t)rt + l % rt;
+  if (gmax >= Tk)
+    return fail(WF_ERR_INVALID_ARGUMENT, "query row map reaches position %lld but only Tk=%lld keys exist",
+                (long long)gmax, (long long)Tk);
+  if (rs == 1 && r0 == 0 && Tq > Tk)
+    return fail(WF_ERR_INVALID_ARGUMENT, "Tq=%lld exceeds Tk=%lld", (long long)Tq, (long long)Tk);
+  return WF_OK;
+}
+
+int check_attn_tensor(const char* name, const void* p, const int64_t* s, int esz) {
+  if (!p || !s) return fail(WF_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (s[3] != 1) return fail(WF_ERR_INVALID_ARGUMENT, "%s: last dimension must be contiguous (stride %lld)", name,
+                             (long long)s[3]);
+  if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
+    return fail(WF_ERR_UNSUPPORTED, "%s: base address must be 16-byte aligned", name);
+  for (int i = 0; i < 3; ++i)
+    if ((s[i] * esz) % 16 != 0)
+      return fail(WF_ERR_UNSUPPORTED, "%s: stride %d (%lld elements) is not a multiple of 16 bytes", name, i,
+                  (long long)s[i]);
+  return WF_OK;
+}
+
+int check_attn(const void* q, const void* k, const void* v, int32_t dtype, const int32_t* idx, int64_t B,
+               int64_t H, int64_t Tq, int64_t Tk, int32_t D, int32_t K, const int64_t* qs,
+               const int64_t* ks, const int64_t* vs, const int64_t* is, float scale, int32_t flags,
+               const void* out, int32_t out_dtype, const int64_t* os) {
+  if (B < 0 || H < 0 || Tq < 0 || Tk < 0 || K < 0)
+    return fail(WF_ERR_INVALID_ARGUMENT, "negative size argument");
+  if (!valid_dtype(dtype)) return fail(WF_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (!valid_dtype(out_dtype)) return fail(WF_ERR_INVALID_ARGUMENT, "unknown out_dtype %d", out_dtype);
+  if (flags & ~WF_ATTN_MASK_NEGATIVE) return fail(WF_ERR_INVALID_ARGUMENT, "unknown flags 0x%x", flags);
+  if (!std::isfinite(scale)) return fail(WF_ERR_INVALID_ARGUMENT, "scale must be finite");
+  if (D != 16 && D != 32 && D != 64 && D != 128 && D != 256)
+    return fail(WF_ERR_UNSUPPORTED, "head_dim D=%d not supported (16, 32, 64, 128, 256)", D);
+  if (Tk > kI32Max || Tq > kI32Max || B > kI32Max || H > kI32Max)
+    return fail(WF_ERR_UNSUPPORTED, "sizes too large");
+  if (B == 0 || H == 0 || Tq == 0) return WF_OK;
+  if (K == 0) return fail(WF_ERR_INVALID_ARGUMENT, "softmax over K=0 retrieved rows is undefined");
+  if (K > wf::attn_max_k())
+    return fail(WF_ERR_UNSUPPORTED, "K=%d exceeds this build's maximum of %d", K, wf::attn_max_k());
+  if (Tk == 0) return fail(WF_ERR_INVALID_ARGUMENT, "no keys to attend to (Tk=0)");
+  if (!idx || !is) return fail(WF_ERR_INVALID_ARGUMENT, "indices: null pointer");
+  const int esz = dtype_size(dtype);
+  int rc;
+  if ((rc = check_attn_tensor("q", q, qs, esz))) return rc;
+  if ((rc = check_attn_tensor("k", k, ks, esz))) return rc;
+  if ((rc = check_attn_tensor("v", v, vs, esz))) return rc;
+  if (!out || !os) return fail(WF_ERR_INVALID_ARGUMENT, "out: null pointer");
+  if (os[3] != 1) return fail(WF_ERR_INVALID_ARGUMENT, "out: last dimension must be contiguous");
+  const int64_t work = B * H * Tq;
+  if ((work + 7) / 8 > kI32Max) return fail(WF_ERR_UNSUPPORTED, "B*H*Tq too large for one launch");
+  return WF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wf_version(void) { return 100; }
+
+const char* wf_last_error(void) { return g_err.c_str(); }
+
+int wf_max_top_k(void) { return wf::topk_max_k(); }
+
+int wf_causal_topk(const void* q_addr, const void* k_addr, int32_t dtype, int64_t B, int64_t Tq,
+                   int64_t Tk, int32_t R, const int64_t* q_strides, const int64_t* k_strides,
+                   int32_t top_k, int32_t pad_mode, int32_t row_tile, int32_t row_stride,
+                   int32_t row_start, int32_t* idx_out, void* stream) {
+  int32_t k_eff = 0;
+  int rc = check_topk(q_addr, k_addr, dtype, B, Tq, Tk, R, q_strides, k_strides, top_k, pad_mode, row_tile,
+                      row_stride, row_start, idx_out, &k_eff);
+  if (rc) return rc;
+  if (k_eff == 0 || B == 0 || Tq == 0) return ok();
+  wf::TopkParams p{};
+  p.q = q_addr;
+  p.k = k_addr;
+  p.qsb = q_strides[0]; p.qst = q_strides[1]; p.qsr = q_strides[2];
+  p.ksb = k_strides[0]; p.kst = k_strides[1]; p.ksr = k_strides[2];
+  p.B = (int)B; p.Tq = (int)Tq; p.Tk = (int)Tk; p.R = R; p.K = k_eff;
+  p.pad_mode = pad_mode;
+  p.rt = row_tile; p.rs = row_stride; p.r0 = row_start;
+  p.idx = idx_out;
+  rc = wf::launch_causal_topk(p, dtype, static_cast<cudaStream_t>(stream));
+  if (rc) return cuda_fail(rc, "wf_causal_topk");
+  return ok();
+}
+
+int wf_sparse_attention(const void* q, const void* k, const void* v, int32_t dtype, const int32_t* idx,
+                        int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t D, int32_t K,
+                        const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                        const int64_t* idx_strides, float scale, int32_t flags, void* out, int32_t out_dtype,
+                        const int64_t* out_strides, int32_t* status, void* stream) {
+  int rc = check_attn(q, k, v, dtype, idx, B, H, Tq, Tk, D, K, q_strides, k_strides, v_strides, idx_strides,
+                      scale, flags, out, out_dtype, out_strides);
+  if (rc) return rc;
+  if (B == 0 || H == 0 || Tq == 0) return ok();
+  wf::AttnParams p{};
+  p.q = q; p.k = k; p.v = v; p.idx = idx; p.out = out;
+  p.qsb = q_strides[0]; p.qsh = q_strides[1]; p.qst = q_strides[2];
+  p.ksb = k_strides[0]; p.ksh = k_strides[1]; p.kst = k_strides[2];
+  p.vsb = v_strides[0]; p.vsh = v_strides[1]; p.vst = v_strides[2];
+  p.osb = out_strides[0]; p.osh = out_strides[1]; p.ost = out_strides[2];
+  p.isb = idx_strides[0]; p.ist = idx_strides[1]; p.iss = idx_strides[2];
+  p.B = (int)B; p.H = (int)H; p.Tq = (int)Tq; p.Tk = (int)Tk; p.D = D; p.K = K;
+  p.scale = scale;
+  p.mask_negative = (flags & WF_ATTN_MASK_NEGATIVE) ? 1 : 0;
+  p.status = status;
+  rc = wf::launch_sparse_attention(p, dtype, out_dtype, static_cast<cudaStream_t>(stream));
+  if (rc) return cuda_fail(rc, "wf_sparse_attention");
+  return ok();
+}
+
+int wf_fused_sparse_attention(const void* q_addr, const void* k_addr, int32_t addr_dtype, int32_t R,
+                              const int64_t* q_addr_strides, const int64_t* k_addr_strides, const void* q,
+                              const void* k, const void* v, int32_t dtype, int64_t B, int64_t H, int64_t Tq,
+                              int64_t Tk, int32_t D, const int64_t* q_strides, const int64_t* k_strides,
+                              const int64_t* v_strides, int32_t top_k, float scale, int32_t pad_mode,
+                              int32_t row_tile, int32_t row_stride, int32_t row_start, int32_t* idx_out,
+                              void* out, int32_t out_dtype, const int64_t* out_strides, int32_t* status,
+                              void* stream) {
+  int32_t k_eff = 0;
+  int32_t rt = row_tile, rs = row_stride, r0 = row_start;
+  int rc = check_topk(q_addr, k_addr, addr_dtype, B, Tq, Tk, R, q_addr_strides, k_addr_strides, top_k, pad_mode,
+                      rt, rs, r0, idx_out, &k_eff);
+  if (rc) return rc;
+  if (B == 0 || H == 0 || Tq == 0) return ok();
+  const int64_t idx_strides[3] = {Tq * (int64_t)k_eff, (int64_t)k_eff, 1};
+  rc = check_attn(q, k, v, dtype, idx_out, B, H, Tq, Tk, D, k_eff, q_strides, k_strides, v_strides, idx_strides,
+                  scale, pad_mode == WF_PAD_MASKED ? WF_ATTN_MASK_NEGATIVE : 0, out, out_dtype, out_strides);
+  if (rc) return rc;
+  rc = wf_causal_topk(q_addr, k_addr, addr_dtype, B, Tq, Tk, R, q_addr_strides, k_addr_strides, top_k, pad_mode,
+                      row_tile, row_stride, row_start, idx_out, stream);
+  if (rc) return rc;
+  return wf_sparse_attention(q, k, v, dtype, idx_out, B, H, Tq, Tk, D, k_eff, q_strides, k_strides, v_strides,
+                             idx_strides, scale, pad_mode == WF_PAD_MASKED ? WF_ATTN_MASK_NEGATIVE : 0, out,
+                             out_dtype, out_strides, status, stream);
+}
+
+}  // extern "C"

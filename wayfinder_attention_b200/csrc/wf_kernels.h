@@ -1,0 +1,55 @@
+// Host-side launch interface between the C ABI (wf_abi.cu) and the kernels.
+// Not part of the public ABI: include/wayfinder.h is.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace wf {
+
+// Causal top-K over address vectors.
+//   query rows:  q[b, l, :]  for local row l in [0, Tq); its sequence position
+//                g(l) = ((l / rt) * rs + r0) * rt + l % rt   (identity when rs=1, r0=0, rt>=Tq)
+//   keys:        k[b, j, :]  for j in [0, Tk); row g may retrieve j <= g only.
+//   output:      idx[(b * Tq + l) * K + s], s = slot (descending score, ties -> lower index)
+struct TopkParams {
+  const void* q;
+  const void* k;
+  int64_t qsb, qst, qsr;
+  int64_t ksb, kst, ksr;
+  int B, Tq, Tk, R, K;
+  int pad_mode;          // 0: reference pads (g + K + s + 1) % Tk; 1: -1 (masked)
+  int rt, rs, r0;        // query row map
+  int32_t* idx;
+  int cap;               // candidate buffer capacity per row (multiple of 32)
+};
+
+// Sparse attention over retrieved rows, indices shared across heads.
+struct AttnParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const int32_t* idx;
+  void* out;
+  int64_t qsb, qsh, qst;
+  int64_t ksb, ksh, kst;
+  int64_t vsb, vsh, vst;
+  int64_t osb, osh, ost;
+  int64_t isb, ist, iss;
+  int B, H, Tq, Tk, D, K;
+  float scale;
+  int mask_negative;     // 1: negative index = masked slot; 0: wraps like torch indexing
+  int32_t* status;       // nullable; bit 0 set on an out-of-range index
+};
+
+// Returns a cudaError_t; a negative value means "unsupported configuration"
+// (the caller formats the message).
+int launch_causal_topk(const TopkParams& p, int dtype, cudaStream_t stream);
+int launch_sparse_attention(const AttnParams& p, int dtype, int out_dtype, cudaStream_t stream);
+
+// Shared-memory bytes the top-K kernel needs for (R, K); 0 if unsupported.
+size_t topk_smem_bytes(int R, int K);
+int topk_max_k();
+int attn_max_k();
+
+}  // namespace wf

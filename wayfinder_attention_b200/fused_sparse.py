@@ -1,0 +1,204 @@
+"""Sparse softmax attention over retrieved rows, and the fused retrieval + attention op.
+
+Drop-in for ``routing_attention.kernels.fused_sparse`` of the reference:
+  * ``sparse_meat_attention``  <- ``fused_sparse.py:275-324``
+  * ``fused_sparse_attention`` <- ``fused_sparse.py:327-356``
+  * ``SparseMeatConfig``       <- ``fused_sparse.py:30-38`` (accepted, ignored)
+
+The arithmetic is that of ``sparse_meat_attention_reference``
+(``fused_sparse.py:80-94``): gather K/V rows at indices shared by all heads,
+scaled dot products, softmax over the K retrieved rows, weighted sum of V,
+evaluated in fp32 and rounded once to the output dtype (the reference's
+``batched`` GPU path runs its softmax in the input dtype instead).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .causal_topk import _launch_topk, pad_mode_code, promote_compute_dtype
+
+
+@dataclass
+class SparseMeatConfig:
+    """Launch tuning of the reference (``fused_sparse.py:30-38``); the CUDA kernel ignores it."""
+
+    method: str = "auto"
+    block_d: int | None = None
+    k_pad: int | None = None
+    num_warps: int = 4
+    compute_dtype: str | None = None
+
+
+def _attn_operand(t: torch.Tensor) -> torch.Tensor:
+    """Return ``t`` if the kernel can read it in place (unit last stride, 16-byte rows), else a compact copy."""
+    esz = t.element_size()
+    ok = (
+        t.stride(-1) == 1
+        and t.data_ptr() % 16 == 0
+        and all((s * esz) % 16 == 0 for s in t.stride()[:-1])
+    )
+    return t if ok else t.contiguous()
+
+
+def _check_meat_shapes(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError(f"expected (B,H,T,D) q/k/v, got {tuple(q.shape)}, {tuple(k.shape)}, {tuple(v.shape)}")
+    if k.shape != v.shape:
+        raise ValueError(f"k/v shape mismatch: {tuple(k.shape)} vs {tuple(v.shape)}")
+    if q.shape[0] != k.shape[0] or q.shape[1] != k.shape[1] or q.shape[3] != k.shape[3]:
+        raise ValueError(f"q/k shape mismatch: {tuple(q.shape)} vs {tuple(k.shape)}")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError(f"q/k/v dtype mismatch: {q.dtype}, {k.dtype}, {v.dtype}")
+
+
+def _launch_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    indices: torch.Tensor,
+    scale: float,
+    *,
+    mask_negative: bool,
+    out_dtype: torch.dtype | None,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    dev = _lib.require_cuda(q, k, v, indices)
+    lib = _lib.load_library()
+    B, H, Tq, D = q.shape
+    Tk = k.shape[2]
+    K = indices.shape[-1]
+    if indices.dim() != 3 or indices.shape[0] != B or indices.shape[1] != Tq:
+        raise ValueError(f"indices must have shape {(B, Tq, K)}, got {tuple(indices.shape)}")
+    out = torch.empty(B, H, Tq, D, dtype=out_dtype or q.dtype, device=dev)
+    if K == 0:
+        # softmax over an empty set: the reference's sum over zero rows is 0
+        return out.zero_()
+    q, k, v = _attn_operand(q), _attn_operand(k), _attn_operand(v)
+    if status is not None and (status.dtype != torch.int32 or not status.is_cuda):
+        raise ValueError("status must be an int32 CUDA tensor")
+    with torch.cuda.device(dev):
+        rc = lib.wf_sparse_attention(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.dtype_code(q.dtype), indices.data_ptr(),
+            B, H, Tq, Tk, D, K,
+            _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(indices),
+            float(scale), _lib.WF_ATTN_MASK_NEGATIVE if mask_negative else 0,
+            out.data_ptr(), _lib.dtype_code(out.dtype), _lib.strides(out),
+            status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
+        )
+    _lib.check(rc)
+    return out
+
+
+@torch.no_grad()
+def sparse_meat_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    indices: torch.Tensor,
+    scale: float,
+    *,
+    method: str = "auto",
+    config: SparseMeatConfig | None = None,
+    out_dtype: torch.dtype | None = None,
+    mask_negative: bool = False,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Multi-head sparse attention on pre-selected indices shared across heads.
+
+    q: (B, H, T, D); k, v: (B, H, Tk, D); indices: (B, T, K) (cast to int32
+    like ``fused_sparse.py:297-298``).  Returns (B, H, T, D) in ``q.dtype``
+    unless ``out_dtype`` is given.  Negative indices wrap by Tk like torch
+    indexing unless ``mask_negative`` is set, in which case they are excluded
+    from the softmax.
+    """
+    del method, config
+    _check_meat_shapes(q, k, v)
+    if q.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        q, k, v = q.float(), k.float(), v.float()
+    if indices.dtype != torch.int32:
+        indices = indices.to(torch.int32)
+    return _launch_attention(q, k, v, indices, scale, mask_negative=mask_negative, out_dtype=out_dtype,
+                             status=status)
+
+
+def sparse_meat_attention_reference(q, k, v, indices, scale):
+    """Name kept from ``fused_sparse.py:80-94``; runs the same CUDA kernel (fp32 arithmetic)."""
+    return sparse_meat_attention(q, k, v, indices, scale, method="reference")
+
+
+@torch.no_grad()
+def fused_sparse_attention(
+    q_search: torch.Tensor,
+    k_search: torch.Tensor,
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    top_k: int,
+    scale: float,
+    *,
+    retrieval_method: str = "auto",
+    meat_method: str = "auto",
+    meat_config: SparseMeatConfig | None = None,
+    pad_mode: str = "reference",
+    out_dtype: torch.dtype | None = None,
+    status: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Causal top-K retrieval + sparse attention: returns (out (B,H,T,D), indices (B,T,K) int32).
+
+    Mirrors ``fused_sparse_attention`` (``routing_attention/kernels/fused_sparse.py:327-356``).
+    ``pad_mode="masked"`` excludes the pad slots of rows ``i < K-1`` from the
+    softmax instead of attending to them as the reference does.
+    """
+    del retrieval_method, meat_method, meat_config
+    if q_search.shape != k_search.shape:
+        raise ValueError(f"query/key shape mismatch: {q_search.shape} vs {k_search.shape}")
+    if q_search.dim() != 3:
+        raise ValueError(f"expected (B,T,R), got {tuple(q_search.shape)}")
+    _check_meat_shapes(q, k, v)
+    B, T, R = q_search.shape
+    if q.shape[0] != B or q.shape[2] != T or k.shape[2] != T:
+        raise ValueError(f"search vectors {tuple(q_search.shape)} do not match q/k/v {tuple(q.shape)}")
+    k_eff = min(int(top_k), T)
+    if k_eff <= 0:
+        idx = torch.zeros(B, T, 0, dtype=torch.int32, device=q.device)
+        return torch.zeros(q.shape, dtype=out_dtype or q.dtype, device=q.device), idx
+    dev = _lib.require_cuda(q_search, k_search, q, k, v)
+    lib = _lib.load_library()
+    qa, ka, _ = promote_compute_dtype(q_search, k_search, None)
+    if q.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        q, k, v = q.float(), k.float(), v.float()
+    q, k, v = _attn_operand(q), _attn_operand(k), _attn_operand(v)
+    H, D = q.shape[1], q.shape[3]
+    idx = torch.empty(B, T, k_eff, dtype=torch.int32, device=dev)
+    out = torch.empty(B, H, T, D, dtype=out_dtype or q.dtype, device=dev)
+    if status is not None and (status.dtype != torch.int32 or not status.is_cuda):
+        raise ValueError("status must be an int32 CUDA tensor")
+    with torch.cuda.device(dev):
+        rc = lib.wf_fused_sparse_attention(
+            qa.data_ptr(), ka.data_ptr(), _lib.dtype_code(qa.dtype), R, _lib.strides(qa), _lib.strides(ka),
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.dtype_code(q.dtype), B, H, T, T, D,
+            _lib.strides(q), _lib.strides(k), _lib.strides(v), int(top_k), float(scale),
+            pad_mode_code(pad_mode), 0, 1, 0, idx.data_ptr(), out.data_ptr(), _lib.dtype_code(out.dtype),
+            _lib.strides(out), status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
+        )
+    _lib.check(rc)
+    return out, idx
+
+
+def fused_sparse_attention_available() -> bool:
+    """True when the CUDA library is built and a GPU is visible (``fused_sparse.py:60-61``)."""
+    return _lib.LIB_PATH.exists() and torch.cuda.is_available()
+
+
+__all__ = [
+    "SparseMeatConfig",
+    "sparse_meat_attention",
+    "sparse_meat_attention_reference",
+    "fused_sparse_attention",
+    "fused_sparse_attention_available",
+    "_launch_topk",
+]
