@@ -198,11 +198,14 @@ def test_topk_exact_ties_break_to_lower_index(cuda_device):
     T, R, K = 512, 32, 16
     g = torch.Generator().manual_seed(3)
     base = torch.randn(8, R, generator=g)
-    ka = base[torch.randint(0, 8, (1, T), generator=g)]
+    sel = torch.randint(0, 8, (1, T), generator=g)
+    ka = base[sel]
     qa = torch.randn(1, T, R, generator=g)
     got = causal_topk(qa.to(cuda_device), ka.to(cuda_device), K).cpu().numpy()
+    sel_np = sel[0].numpy()
     for i in range(K - 1, T):
-        s = oracle.exact_scores_f64(qa.numpy(), ka.numpy(), 0, i)  # equal keys -> bitwise equal scores
+        # score each distinct base vector once, so duplicated keys get bitwise-equal scores
+        s = (base.double().numpy() @ qa[0, i].double().numpy())[sel_np[: i + 1]]
         want = np.lexsort((np.arange(i + 1), -s))[:K]
         assert got[0, i].tolist() == want.tolist(), i
 
@@ -256,7 +259,7 @@ def test_attention_index_semantics(cuda_device):
     out = sparse_meat_attention(x["q"], x["k"], x["v"], idx.to(cuda_device), 0.125, out_dtype=torch.float32)
     want = oracle.sparse_meat_attention(xn["q"], xn["k"], xn["v"], idx.numpy(), 0.125)
     assert np.abs(_np(out) - want).max() <= 1e-5
-    idx[..., 0] = idx[..., 0].abs()
+    idx[..., 0] = idx[..., 0] % w.T  # keep one real key per row
     out = sparse_meat_attention(x["q"], x["k"], x["v"], idx.to(cuda_device), 0.125, out_dtype=torch.float32,
                                 mask_negative=True)
     want = oracle.sparse_meat_attention(xn["q"], xn["k"], xn["v"], idx.numpy(), 0.125, mask_negative=True)
@@ -333,3 +336,31 @@ def test_decoder_prefill_smoke(cuda_device):
     with torch.no_grad():
         logits = m(ids)["logits"]
     assert logits.shape == (2, 512, 128) and torch.isfinite(logits).all()
+
+
+@pytest.mark.parametrize(
+    "R,K,T,B,dtype,clustered",
+    [
+        (32, 128, 16384, 1, torch.bfloat16, False),
+        (32, 128, 4096, 2, torch.bfloat16, True),
+        (16, 64, 1000, 2, torch.float16, False),
+        (64, 128, 3000, 1, torch.bfloat16, False),
+        (32, 32, 777, 3, torch.bfloat16, True),
+        (32, 1, 300, 1, torch.bfloat16, False),
+        (32, 128, 130, 1, torch.bfloat16, False),
+    ],
+)
+def test_tensor_core_topk_equals_cuda_core(R, K, T, B, dtype, clustered, cuda_device, monkeypatch):
+    """The tcgen05 scorer admits keys on tensor-core scores but ranks on exact fp32 rescoring,
+    so it must return exactly what the CUDA-core kernel returns."""
+    w = Workload("t", B, 1, T, 16, R, K, dtype, clustered=clustered)
+    x = to_device(make_inputs(w), cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    tc = causal_topk(x["q_addr"], x["k_addr"], K)
+    monkeypatch.setenv("WF_TOPK_IMPL", "cuda_core")
+    cc = causal_topk(x["q_addr"], x["k_addr"], K)
+    monkeypatch.delenv("WF_TOPK_IMPL")
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    mism = (tc != cc).any(dim=-1)
+    assert not mism.any(), f"{int(mism.sum())} rows differ, first {torch.nonzero(mism)[:5].tolist()}"

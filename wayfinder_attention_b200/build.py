@@ -22,7 +22,7 @@ CSRC = PKG_DIR / "csrc"
 LIB_NAME = "libwayfinder_sm100.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["wf_abi.cu", "wf_topk.cu", "wf_attn.cu"]
+SOURCES = ["wf_abi.cu", "wf_topk.cu", "wf_topk_tc.cu", "wf_attn.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

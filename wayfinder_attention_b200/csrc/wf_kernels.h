@@ -22,6 +22,7 @@ struct TopkParams {
   int rt, rs, r0;        // query row map
   int32_t* idx;
   int cap;               // candidate buffer capacity per row (multiple of 32)
+  int32_t* status;       // nullable; bit 1 set if a bounded wait timed out
 };
 
 // Sparse attention over retrieved rows, indices shared across heads.
@@ -46,6 +47,11 @@ struct AttnParams {
 // (the caller formats the message).
 int launch_causal_topk(const TopkParams& p, int dtype, cudaStream_t stream);
 int launch_sparse_attention(const AttnParams& p, int dtype, int out_dtype, cudaStream_t stream);
+
+// Tensor-core (tcgen05) top-K: bf16/fp16 addresses, R in {16, 32, 64}, K <= 128,
+// Tk <= 65536, unit address stride, 16-byte aligned rows.
+bool topk_tc_supported(const TopkParams& p, int dtype);
+int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream);
 
 // Shared-memory bytes the top-K kernel needs for (R, K); 0 if unsupported.
 size_t topk_smem_bytes(int R, int K);

@@ -21,126 +21,23 @@
 // find the exact K-th value and compacts the buffer back to K entries.
 #include "wf_common.cuh"
 #include "wf_kernels.h"
+#include "wf_select.cuh"
 
 #include <climits>
+#include <cstdlib>
+#include <cstring>
 
 namespace wf {
 namespace {
+
+using select::merge_row;
+using select::bitonic_sort_desc;
 
 constexpr int kRows = 64;      // query rows per CTA
 constexpr int kChunk = 64;     // keys per streamed chunk
 constexpr int kThreads = 256;
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kMaxDevices = 64;
-
-// Select the exact top-K (by ordered key, ties -> lower index) among the n > K
-// entries of one row's buffer and compact them to positions [0, K).
-// Returns the K-th key, the new admission threshold.
-template <int EPL>
-__device__ __forceinline__ uint32_t merge_row(uint32_t* bk, int* bi, int n, int K, int lane) {
-  uint32_t kk[EPL];
-  int ii[EPL];
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    const int e = i * 32 + lane;
-    const bool in = e < n;
-    kk[i] = in ? bk[e] : 0u;
-    ii[i] = in ? bi[e] : INT_MAX;
-  }
-  // tau = largest value with #(key >= tau) >= K, i.e. the K-th largest key.
-  uint32_t tau = 0;
-#pragma unroll 1
-  for (int bit = 31; bit >= 0; --bit) {
-    const uint32_t cand = tau | (1u << bit);
-    unsigned c = 0;
-#pragma unroll
-    for (int i = 0; i < EPL; ++i) c += (kk[i] >= cand) ? 1u : 0u;
-    c = __reduce_add_sync(kFull, c);
-    if (c >= (unsigned)K) tau = cand;
-  }
-  unsigned gt = 0, eq = 0;
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    gt += (kk[i] > tau) ? 1u : 0u;
-    eq += (kk[i] == tau) ? 1u : 0u;
-  }
-  gt = __reduce_add_sync(kFull, gt);
-  eq = __reduce_add_sync(kFull, eq);
-  const unsigned need = (unsigned)K - gt;  // 1 <= need <= eq
-  int lim = INT_MAX;                        // keep tied entries with index <= lim
-  if (need < eq) {
-    int last = -1;
-#pragma unroll 1
-    for (unsigned t = 0; t < need; ++t) {
-      int m = INT_MAX;
-#pragma unroll
-      for (int i = 0; i < EPL; ++i)
-        if (kk[i] == tau && ii[i] > last) m = min(m, ii[i]);
-      last = __reduce_min_sync(kFull, m);
-    }
-    lim = last;
-  }
-  __syncwarp();
-  unsigned base = 0;
-  const unsigned lt = lanemask_lt();
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    const bool take = kk[i] > tau || (kk[i] == tau && ii[i] <= lim);
-    const unsigned m = __ballot_sync(kFull, take);
-    if (take) {
-      const unsigned pos = base + __popc(m & lt);
-      bk[pos] = kk[i];
-      bi[pos] = ii[i];
-    }
-    base += __popc(m);
-  }
-  __syncwarp();
-  return tau;
-}
-
-__device__ __forceinline__ uint64_t shfl_xor64(uint64_t v, int o) {
-  const uint32_t lo = __shfl_xor_sync(kFull, (uint32_t)v, o);
-  const uint32_t hi = __shfl_xor_sync(kFull, (uint32_t)(v >> 32), o);
-  return ((uint64_t)hi << 32) | lo;
-}
-
-// Warp bitonic sort, descending, of 32*SE 64-bit values; element e lives in
-// register e / 32 of lane e % 32.
-template <int SE>
-__device__ __forceinline__ void bitonic_sort_desc(uint64_t (&c)[SE], int lane) {
-  constexpr int S = 32 * SE;
-#pragma unroll
-  for (int size = 2; size <= S; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      if (stride >= 32) {
-        const int rs = stride >> 5;
-#pragma unroll
-        for (int i = 0; i < SE; ++i) {
-          if ((i & rs) == 0) {
-            const int j = i | rs;
-            const int e = i * 32 + lane;
-            const bool desc = (e & size) == 0;
-            const uint64_t a = c[i], b = c[j];
-            const bool sw = desc ? (a < b) : (a > b);
-            c[i] = sw ? b : a;
-            c[j] = sw ? a : b;
-          }
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < SE; ++i) {
-          const int e = i * 32 + lane;
-          const uint64_t o = shfl_xor64(c[i], stride);
-          const bool lower = (lane & stride) == 0;
-          const bool desc = (e & size) == 0;
-          const bool keep_max = (lower == desc);
-          c[i] = keep_max ? (c[i] > o ? c[i] : o) : (c[i] < o ? c[i] : o);
-        }
-      }
-    }
-  }
-}
 
 template <typename TI, int RP, int EPL, int SE>
 __global__ void __launch_bounds__(kThreads, 1) causal_topk_kernel(const TopkParams p) {
@@ -349,6 +246,10 @@ size_t topk_smem_bytes(int R, int K) {
 int topk_max_k() { return 256; }
 
 int launch_causal_topk(const TopkParams& p, int dtype, cudaStream_t stream) {
+  // WF_TOPK_IMPL=cuda_core forces the CUDA-core scorer (used by the tests to cross-check the two kernels).
+  const char* impl = getenv("WF_TOPK_IMPL");
+  const bool force_cc = impl && strcmp(impl, "cuda_core") == 0;
+  if (!force_cc && topk_tc_supported(p, dtype)) return launch_causal_topk_tc(p, dtype, stream);
   if (topk_smem_bytes(p.R, p.K) == 0) return -1;
   switch (dtype) {
     case kBF16: return launch_ti<__nv_bfloat16>(p, stream);
