@@ -74,11 +74,13 @@ WF_API int wf_max_top_k(void);
  *             query-row-sharded long sequence addresses its cyclic row blocks.
  *   idx_out : (B, Tq, K_eff) int32, contiguous.  Slots hold the retrieved key indices in
  *             descending score order; equal scores break to the lower index.
+ *   status  : optional device int32; bit 1 is OR-ed in if a bounded internal wait of the
+ *             tensor-core kernel timed out (the output is then invalid).  May be NULL.
  */
 WF_API int wf_causal_topk(const void* q_addr, const void* k_addr, int32_t dtype, int64_t B, int64_t Tq,
                    int64_t Tk, int32_t R, const int64_t* q_strides, const int64_t* k_strides,
                    int32_t top_k, int32_t pad_mode, int32_t row_tile, int32_t row_stride,
-                   int32_t row_start, int32_t* idx_out, void* stream);
+                   int32_t row_start, int32_t* idx_out, int32_t* status, void* stream);
 
 /*
  * Softmax attention over the K rows named by idx, shared by all heads.  Replaces

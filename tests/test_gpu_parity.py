@@ -356,7 +356,7 @@ def test_tensor_core_topk_equals_cuda_core(R, K, T, B, dtype, clustered, cuda_de
     w = Workload("t", B, 1, T, 16, R, K, dtype, clustered=clustered)
     x = to_device(make_inputs(w), cuda_device)
     status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
-    tc = causal_topk(x["q_addr"], x["k_addr"], K)
+    tc = causal_topk(x["q_addr"], x["k_addr"], K, status=status)
     monkeypatch.setenv("WF_TOPK_IMPL", "cuda_core")
     cc = causal_topk(x["q_addr"], x["k_addr"], K)
     monkeypatch.delenv("WF_TOPK_IMPL")

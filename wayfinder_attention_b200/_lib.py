@@ -62,7 +62,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.wf_max_top_k.argtypes = []
     lib.wf_causal_topk.restype = ctypes.c_int
     lib.wf_causal_topk.argtypes = [
-        _vp, _vp, _i32, _i64, _i64, _i64, _i32, _i64p, _i64p, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
+        _vp, _vp, _i32, _i64, _i64, _i64, _i32, _i64p, _i64p, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
     ]
     lib.wf_sparse_attention.restype = ctypes.c_int
     lib.wf_sparse_attention.argtypes = [

@@ -67,6 +67,7 @@ def _launch_topk(
     row_stride: int = 1,
     row_start: int = 0,
     out: torch.Tensor | None = None,
+    status: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Run ``wf_causal_topk`` on (B, Tq, R) queries against (B, Tk, R) keys."""
     dev = _lib.require_cuda(q, k)
@@ -82,7 +83,8 @@ def _launch_topk(
         rc = lib.wf_causal_topk(
             q.data_ptr(), k.data_ptr(), _lib.dtype_code(q.dtype), B, Tq, Tk, R,
             _lib.strides(q), _lib.strides(k), int(top_k), pad_mode_code(pad_mode),
-            int(row_tile), int(row_stride), int(row_start), out.data_ptr(), _lib.stream_ptr(dev),
+            int(row_tile), int(row_stride), int(row_start), out.data_ptr(),
+            status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
         )
     _lib.check(rc)
     return out
@@ -98,6 +100,7 @@ def causal_topk(
     dtype: str | None = None,
     prefer_triton: bool = False,
     pad_mode: str = "reference",
+    status: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Causal top-K retrieval: (B, T, R) x (B, T, R) -> (B, T, min(top_k, T)) int32.
 
@@ -115,7 +118,7 @@ def causal_topk(
         return torch.zeros(B, T, 0, dtype=torch.int32, device=query.device)
     _lib.require_cuda(query, key)
     q, k, _ = promote_compute_dtype(query, key, dtype)
-    return _launch_topk(q, k, top_k, pad_mode)
+    return _launch_topk(q, k, top_k, pad_mode, status=status)
 
 
 def causal_topk_reference(query: torch.Tensor, key: torch.Tensor, top_k: int) -> torch.Tensor:

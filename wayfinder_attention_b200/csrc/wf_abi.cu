@@ -136,7 +136,7 @@ int wf_max_top_k(void) { return wf::topk_max_k(); }
 int wf_causal_topk(const void* q_addr, const void* k_addr, int32_t dtype, int64_t B, int64_t Tq,
                    int64_t Tk, int32_t R, const int64_t* q_strides, const int64_t* k_strides,
                    int32_t top_k, int32_t pad_mode, int32_t row_tile, int32_t row_stride,
-                   int32_t row_start, int32_t* idx_out, void* stream) {
+                   int32_t row_start, int32_t* idx_out, int32_t* status, void* stream) {
   int32_t k_eff = 0;
   int rc = check_topk(q_addr, k_addr, dtype, B, Tq, Tk, R, q_strides, k_strides, top_k, pad_mode, row_tile,
                       row_stride, row_start, idx_out, &k_eff);
@@ -151,6 +151,7 @@ int wf_causal_topk(const void* q_addr, const void* k_addr, int32_t dtype, int64_
   p.pad_mode = pad_mode;
   p.rt = row_tile; p.rs = row_stride; p.r0 = row_start;
   p.idx = idx_out;
+  p.status = status;
   rc = wf::launch_causal_topk(p, dtype, static_cast<cudaStream_t>(stream));
   if (rc) return cuda_fail(rc, "wf_causal_topk");
   return ok();
@@ -200,7 +201,7 @@ int wf_fused_sparse_attention(const void* q_addr, const void* k_addr, int32_t ad
                   scale, pad_mode == WF_PAD_MASKED ? WF_ATTN_MASK_NEGATIVE : 0, out, out_dtype, out_strides);
   if (rc) return rc;
   rc = wf_causal_topk(q_addr, k_addr, addr_dtype, B, Tq, Tk, R, q_addr_strides, k_addr_strides, top_k, pad_mode,
-                      row_tile, row_stride, row_start, idx_out, stream);
+                      row_tile, row_stride, row_start, idx_out, status, stream);
   if (rc) return rc;
   return wf_sparse_attention(q, k, v, dtype, idx_out, B, H, Tq, Tk, D, k_eff, q_strides, k_strides, v_strides,
                              idx_strides, scale, pad_mode == WF_PAD_MASKED ? WF_ATTN_MASK_NEGATIVE : 0, out,

@@ -14,17 +14,12 @@ constexpr unsigned kFull = 0xffffffffu;
 // Select the exact top-K (by ordered key, ties -> lower index) among the n > K
 // entries of one row's buffer and compact them to positions [0, K).
 // Returns the K-th key, the new admission threshold.
+// Register form: kk/ii hold n > K candidates spread as element e = i*32 + lane
+// (empty slots: key 0).  Writes the exact top-K (ties -> lower index) to
+// bk/bi[0, K) and returns the K-th key.
 template <int EPL, typename IdxT>
-__device__ __forceinline__ uint32_t merge_row(uint32_t* bk, IdxT* bi, int n, int K, int lane) {
-  uint32_t kk[EPL];
-  int ii[EPL];
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    const int e = i * 32 + lane;
-    const bool in = e < n;
-    kk[i] = in ? bk[e] : 0u;
-    ii[i] = in ? (int)bi[e] : INT_MAX;
-  }
+__device__ __forceinline__ uint32_t select_compact(const uint32_t (&kk)[EPL], const int (&ii)[EPL], int n, int K,
+                                                   int lane, uint32_t* bk, IdxT* bi) {
   // tau = largest value with #(key >= tau) >= K, i.e. the K-th largest key.
   // It shares every bit above the highest bit in which min and max differ.
   uint32_t mn = 0xffffffffu, mx = 0u;
@@ -87,6 +82,21 @@ __device__ __forceinline__ uint32_t merge_row(uint32_t* bk, IdxT* bi, int n, int
   }
   __syncwarp();
   return tau;
+}
+
+template <int EPL, typename IdxT>
+__device__ __forceinline__ uint32_t merge_row(uint32_t* bk, IdxT* bi, int n, int K, int lane) {
+  uint32_t kk[EPL];
+  int ii[EPL];
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = i * 32 + lane;
+    const bool in = e < n;
+    kk[i] = in ? bk[e] : 0u;
+    ii[i] = in ? (int)bi[e] : INT_MAX;
+  }
+  __syncwarp();
+  return select_compact<EPL, IdxT>(kk, ii, n, K, lane, bk, bi);
 }
 
 __device__ __forceinline__ uint64_t shfl_xor64(uint64_t v, int o) {

@@ -5,24 +5,37 @@
 // row g, the K keys j <= g with the largest fp32 score <q_g, k_j>, slots in
 // descending score order with ties to the lower index, pad slots for short rows.
 //
-// Structure of one CTA (128 query rows = the 128 TMEM lanes, 5 warps):
-//   warp 4 (producer): TMA-loads the q tile once and streams key chunks of 128
-//     rows into a ring of shared-memory stages; one lane issues
-//     tcgen05.mma (M=128, N=128, K=16 per instruction, fp32 accumulate) into a
-//     ring of TMEM accumulators and commits to the chunk's mbarrier; the warp
-//     also records the chunk's max |k| for the error margin below.
-//   warps 0-3 (selection): thread t owns query row t and TMEM lane t.  It reads
-//     its 128 scores of a chunk with tcgen05.ld and admits a key when the
-//     tensor-core score reaches (threshold - margin).  Admitted keys are
-//     rescored exactly in fp32 (sequential FMA over d, the same arithmetic as the
-//     CUDA-core kernel) from the staged key rows, and only that exact score
-//     enters the row's candidate buffer in shared memory.  When a buffer nears
-//     capacity, the warp compacts that row to its exact top-K (radix select),
-//     which raises the row's threshold.
+// Work split.  A tile of 128 query rows (the 128 TMEM lanes) is handled by a
+// cluster of two CTAs on two SMs; CTA rank r streams the key chunks c = r, r+2,
+// ... (128 keys each), so the long rows at the end of the causal triangle are
+// shared by two SMs.  Each CTA has 5 warps: warp 4 TMA-loads the q tile and the
+// key chunks into a shared-memory ring and one of its lanes issues tcgen05.mma
+// (M=128, N=128, K=16 per instruction, fp32 accumulate) into a 2-deep TMEM
+// accumulator ring; warps 0-3 own one query row per thread.
+//
+// Selection is two passes over the CTA's chunks (the MMAs are recomputed; they
+// are nearly free):
+//   pass 1  each thread keeps, in 256 TMEM columns of its lane, the maximum
+//           tensor-core score of each of 256 key groups (group = key position
+//           within a 256-key window of the CTA's stream).  The K-th largest of
+//           those 256 group maxima is the score of K distinct keys, so it lower-
+//           bounds the row's K-th best score.  The two CTAs exchange this bound
+//           through distributed shared memory and keep the larger.
+//   pass 2  a key is admitted when its tensor-core score reaches
+//           (bound - margin); about 1.4 K keys per row are admitted.  Admitted
+//           keys are queued per warp and rescored exactly in fp32 by all 32
+//           lanes together (sequential FMA over d from the q tile and the staged
+//           key rows: the arithmetic of the CUDA-core kernel), then appended to
+//           the row's candidate buffer.  A full buffer is compacted to its exact
+//           top-K (warp radix select), which raises the admission threshold.
+//   merge   each CTA reduces its rows to their exact top-K; CTA r then merges
+//           its own and its peer's candidates (read through DSMEM) for rows
+//           [64r, 64r+64), sorts them and writes the output.
 // The margin, 2^-13 * sum_d |q_d| * max|k|, exceeds any plausible accumulation
-// error of a 32-term fp32 dot product with exact products (the error bound is
-// ~2^-18 of sum |q_d k_d|), so no key whose exact score beats the threshold is
-// ever filtered out: the selection is exact with respect to the fp32 scores.
+// error of a 32-term fp32 dot product with exact bf16/fp16 products, so every
+// key whose exact score reaches the K-th best is admitted: the result is exact
+// with respect to the fp32 scores.  Every wait is bounded; a timeout sets bit 1
+// of the status word (plus one bit, 4..2048, naming the wait site) instead of hanging.
 #include "wf_common.cuh"
 #include "wf_kernels.h"
 #include "wf_select.cuh"
@@ -36,18 +49,22 @@ namespace {
 using namespace sm100;
 using select::bitonic_sort_desc;
 using select::merge_row;
+using select::select_compact;
 
-constexpr int kM = 128;   // query rows per CTA = TMEM lanes
+constexpr int kM = 128;   // query rows per tile = TMEM lanes
 constexpr int kN = 128;   // keys per chunk = MMA N
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = (kEpiWarps + 1) * 32;
+constexpr int kGroups = 256;  // pass-1 key groups per row (TMEM columns 256..511)
+constexpr int kQcap = 1024;   // rescoring queue entries per warp
 constexpr unsigned kFullMask = 0xffffffffu;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr float kEpsScale = 1.0f / 8192.0f;
 constexpr int kMaxDevices = 64;
+constexpr size_t kMaxSmem = 232448;
 
 struct TcParams {
-  const void* q;  // for the exact rescoring of admitted keys
+  const void* q;
   int64_t qsb, qst;
   int B, Tq, Tk, K;
   int pad_mode;
@@ -56,48 +73,63 @@ struct TcParams {
   int32_t* status;
 };
 
-constexpr int stages_for(int R) { return R >= 64 ? 2 : 4; }
-
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 template <int R, int EPL>
 struct Layout {
   static constexpr int ROWB = R * 2;
-  static constexpr int S = stages_for(R);
+  static constexpr int S = R >= 64 ? 2 : 3;  // shared-memory stages
   static constexpr int CAP = 32 * EPL;
   static constexpr size_t Q_BYTES = (size_t)kM * ROWB;
   static constexpr size_t STAGE_BYTES = (size_t)kN * ROWB;
+  static constexpr size_t STAGE_STRIDE = align_up(STAGE_BYTES, 1024);
   static constexpr size_t off_q = 0;
   static constexpr size_t off_k = align_up(Q_BYTES, 1024);
-  static constexpr size_t off_kmax = off_k + S * align_up(STAGE_BYTES, 1024);
+  static constexpr size_t off_kmax = off_k + S * STAGE_STRIDE;
   static constexpr size_t off_bar = align_up(off_kmax + sizeof(float) * S, 8);
-  static constexpr size_t n_bar = 3 * S + 1;
-  static constexpr size_t off_misc = off_bar + 8 * n_bar;  // tmem base, abort flag
-  static constexpr size_t off_bkey = align_up(off_misc + 16, 16);
-  static constexpr size_t KEY_STRIDE = CAP + 1;  // words; odd stride keeps row-private appends conflict-free
+  static constexpr size_t n_bar = 3 * S + 4;  // full, mdone, done, qbar, xbar, rbar, dbar
+  static constexpr size_t off_misc = off_bar + 8 * n_bar;  // tmem base, kmax own, kmax peer, abort
+  static constexpr size_t off_theta = align_up(off_misc + 16, 16);
+  static constexpr size_t off_cnt = off_theta + 4 * kM;
+  static constexpr size_t off_queue = off_cnt + 4 * kM;
+  static constexpr size_t off_bkey = off_queue + 4 * (size_t)kQcap * kEpiWarps;
+  static constexpr size_t KEY_STRIDE = CAP + 1;  // words: odd stride keeps row-private appends conflict-free
   static constexpr size_t IDX_STRIDE = CAP + 2;  // halfwords
   static constexpr size_t off_bidx = off_bkey + sizeof(uint32_t) * kM * KEY_STRIDE;
   static constexpr size_t bytes = off_bidx + sizeof(uint16_t) * kM * IDX_STRIDE;
-  static constexpr size_t smem = bytes + 1024;  // slack to align the dynamic base
+  static constexpr size_t smem = bytes + 1024;  // slack to align the dynamic base to 1024
 };
 
-template <typename TI>
-__device__ __forceinline__ float rescore(const float* qf, const unsigned char* row, int j, int rowb) {
-  // Key row j of a stage stored with the TMA swizzle matching `rowb` (32/64/128 B):
-  // 16-byte chunk c lives at chunk c ^ ((j * rowb >> 7) & (rowb / 16 - 1)).
-  const int sw = (j * rowb >> 7) & (rowb / 16 - 1);
+// Exact fp32 score of q-tile row qr and stage row kr, both stored with the TMA
+// swizzle of `ROWB`-byte rows: 16-byte chunk c of row j sits at c ^ ((j*ROWB >> 7) & (ROWB/16 - 1)).
+// A wait that every lane of the warp performs; the verdict is made warp-uniform
+// so a timeout never leaves the warp diverged in front of warp-synchronous code.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, kWaitLimitNs));
+}
+__device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait_cluster(bar, parity, kWaitLimitNs));
+}
+
+template <typename TI, int ROWB>
+__device__ __forceinline__ float dot_swizzled(const unsigned char* qtile, int qr, const unsigned char* stage, int kr) {
+  const int swq = (qr * ROWB >> 7) & (ROWB / 16 - 1);
+  const int swk = (kr * ROWB >> 7) & (ROWB / 16 - 1);
+  const unsigned char* qrow = qtile + qr * ROWB;
+  const unsigned char* krow = stage + kr * ROWB;
   float acc = 0.f;
-  for (int c = 0; c < rowb / 16; ++c) {
-    const uint4 w = *reinterpret_cast<const uint4*>(row + ((c ^ sw) << 4));
-    float f[8];
-    Vec16<TI>::unpack(w, f);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc = fmaf(qf[c * 8 + e], f[e], acc);
+  for (int c = 0; c < ROWB / 16; ++c) {
+    float a[8], b[8];
+    Vec16<TI>::unpack(*reinterpret_cast<const uint4*>(qrow + ((c ^ swq) << 4)), a);
+    Vec16<TI>::unpack(*reinterpret_cast<const uint4*>(krow + ((c ^ swk) << 4)), b);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc = fmaf(a[e], b[e], acc);
   }
   return acc;
 }
 
-template <typename TI, int R, int EPL, int SE>
+template <typename TI, int R, int EPL, int SE, int EPLF>
 __global__ void __launch_bounds__(kThreads, 1)
     causal_topk_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                           const TcParams p) {
@@ -107,40 +139,55 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int CAP = L::CAP;
   constexpr int KSTEPS = R / 16;
   constexpr uint32_t TMEM_COLS = 512;
-  constexpr uint32_t IDESC = idesc_f16(sizeof(TI) == 2 && !std::is_same<TI, __half>::value, kM, kN);
+  constexpr bool kBf16 = !std::is_same<TI, __half>::value;
+  constexpr uint32_t IDESC = idesc_f16(kBf16, kM, kN);
 
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* base =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* qs = base + L::off_q;
   unsigned char* ks = base + L::off_k;
-  float* kmax_s = reinterpret_cast<float*>(base + L::off_kmax);
   uint64_t* full = reinterpret_cast<uint64_t*>(base + L::off_bar);
   uint64_t* mdone = full + S;
-  uint64_t* empty = mdone + S;
-  uint64_t* qbar = empty + S;
+  uint64_t* done = mdone + S;
+  uint64_t* qbar = done + S;
+  uint64_t* xbar = qbar + 1;  // peer posted its pass-1 bound
+  uint64_t* rbar = qbar + 2;  // peer's candidate buffers are final
+  uint64_t* dbar = qbar + 3;  // peer finished reading our buffers
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(base + L::off_misc);
-  int* abort_s = reinterpret_cast<int*>(base + L::off_misc + 4);
+  uint32_t* kmax_own_s = tmem_base_s + 1;
+  uint32_t* kmax_in_s = tmem_base_s + 2;
+  float* theta_in = reinterpret_cast<float*>(base + L::off_theta);
+  int* cnt_s = reinterpret_cast<int*>(base + L::off_cnt);
+  uint32_t* queues = reinterpret_cast<uint32_t*>(base + L::off_queue);
   uint32_t* bkey = reinterpret_cast<uint32_t*>(base + L::off_bkey);
   uint16_t* bidx = reinterpret_cast<uint16_t*>(base + L::off_bidx);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t peer = rank ^ 1u;
   const int ntile = (p.Tq + kM - 1) / kM;
-  const int tile = ntile - 1 - (int)blockIdx.x;  // heaviest tiles first
+  const int tile = ntile - 1 - (int)(blockIdx.x >> 1);  // heaviest tiles first
   const int b = blockIdx.y;
   const int l0 = tile * kM;
   const int nrows = min(kM, p.Tq - l0);
   const int g0 = ((l0 / p.rt) * p.rs + p.r0) * p.rt + (l0 % p.rt);
   const int key_end = min(g0 + nrows, p.Tk);
   const int nchunks = (key_end + kN - 1) / kN;
+  const int n_own = nchunks > (int)rank ? (nchunks - (int)rank + 1) / 2 : 0;
+  const int n_work = 2 * n_own;
 
   if (warp == kEpiWarps && lane == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&mdone[s], 2);
-      mbar_init(&empty[s], kEpiWarps);
+      mbar_init(&done[s], kEpiWarps);
     }
     mbar_init(qbar, 1);
-    *abort_s = 0;
+    mbar_init(xbar, kM);
+    mbar_init(rbar, kM);
+    mbar_init(dbar, kM);
+    *kmax_own_s = 0u;
     fence_mbarrier_init();
   }
   if (warp == 0) {
@@ -148,32 +195,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any peer arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_s;
+  bool ok = true;
+  uint32_t why = 0;  // wait sites that timed out (status bits 4..)
+
+  auto chunk_of = [&](int w) { return (int)rank + 2 * (w % n_own); };
 
   if (warp == kEpiWarps) {
-    // ------------------------------------------------------------ producer
-    bool ok = true;
+    // ============================================================ producer
     if (lane == 0) {
       prefetch_tmap(&qmap);
       prefetch_tmap(&kmap);
       mbar_arrive_expect_tx(qbar, (uint32_t)L::Q_BYTES);
       tma_load_3d(qs, &qmap, qbar, 0, l0, b);
-      for (int c = 0; c < min(S, nchunks); ++c) {
-        mbar_arrive_expect_tx(&full[c], (uint32_t)L::STAGE_BYTES);
-        tma_load_3d(ks + c * align_up(L::STAGE_BYTES, 1024), &kmap, &full[c], 0, c * kN, b);
+      for (int w = 0; w < min(S, n_work); ++w) {
+        mbar_arrive_expect_tx(&full[w], (uint32_t)L::STAGE_BYTES);
+        tma_load_3d(ks + w * L::STAGE_STRIDE, &kmap, &full[w], 0, chunk_of(w) * kN, b);
       }
     }
-    ok = mbar_wait(qbar, 0, kWaitLimitNs);
-    for (int c = 0; c < nchunks && ok; ++c) {
-      const int s = c % S;
-      const uint32_t ph = (uint32_t)(c / S) & 1u;
-      unsigned char* stage = ks + s * align_up(L::STAGE_BYTES, 1024);
-      if (!mbar_wait(&full[s], ph, kWaitLimitNs)) { ok = false; break; }
+    ok = warp_wait(qbar, 0);
+    if (!ok) why |= 4;
+    uint32_t kbits = 0;
+    for (int w = 0; w < n_work && ok; ++w) {
+      const int s = w % S;
+      unsigned char* stage = ks + s * L::STAGE_STRIDE;
+      if (!warp_wait(&full[s], (uint32_t)(w / S) & 1u)) { ok = false; why |= 8; break; }
+      // accumulator (w & 1) was last read by item w-2
+      if (w >= 2 && !warp_wait(&done[(w - 2) % S], (uint32_t)((w - 2) / S) & 1u)) { ok = false; why |= 16; break; }
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t d = tmem_base + (uint32_t)(s * kN);
+        const uint32_t d = tmem_base + (uint32_t)((w & 1) * kN);
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; ++kk) {
           const uint64_t a = smem_desc_kmajor(smem_u32(qs) + kk * 32, ROWB);
@@ -182,158 +235,330 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(&mdone[s]);
       }
-      // max |k| over the staged rows (bit patterns of non-negative floats order like values)
-      uint32_t m2 = 0;
-      const uint4* v = reinterpret_cast<const uint4*>(stage);
-      for (int i = lane; i < (int)(L::STAGE_BYTES / 16); i += 32) {
-        const uint4 w = v[i];
-        m2 = __vmaxu2(m2, w.x & 0x7fff7fffu);
-        m2 = __vmaxu2(m2, w.y & 0x7fff7fffu);
-        m2 = __vmaxu2(m2, w.z & 0x7fff7fffu);
-        m2 = __vmaxu2(m2, w.w & 0x7fff7fffu);
+      if (w < n_own) {
+        // max |k| over the chunk (bit patterns of non-negative floats order like values)
+        const uint4* v = reinterpret_cast<const uint4*>(stage);
+        uint32_t m2 = 0;
+        for (int i = lane; i < (int)(L::STAGE_BYTES / 16); i += 32) {
+          const uint4 x = v[i];
+          m2 = __vmaxu2(m2, x.x & 0x7fff7fffu);
+          m2 = __vmaxu2(m2, x.y & 0x7fff7fffu);
+          m2 = __vmaxu2(m2, x.z & 0x7fff7fffu);
+          m2 = __vmaxu2(m2, x.w & 0x7fff7fffu);
+        }
+        kbits = max(kbits, __reduce_max_sync(kFullMask, max(m2 & 0xffffu, m2 >> 16)));
+        if (w == n_own - 1 && lane == 0) {
+          const float km = kBf16 ? __uint_as_float(kbits << 16) : __half2float(__ushort_as_half((unsigned short)kbits));
+          *kmax_own_s = __float_as_uint(km);
+        }
       }
-      uint32_t mb = max(m2 & 0xffffu, m2 >> 16);
-      mb = __reduce_max_sync(kFullMask, mb);
-      if (lane == 0) {
-        float km;
-        if (std::is_same<TI, __half>::value) km = __half2float(__ushort_as_half((unsigned short)mb));
-        else km = __uint_as_float(mb << 16);
-        kmax_s[s] = km;
-        mbar_arrive(&mdone[s]);
-      }
-      // refill the stage that chunk c-1 used once its consumers are done
-      const int cn = c - 1 + S;
-      if (c >= 1 && cn < nchunks) {
-        const int s1 = (c - 1) % S;
-        if (!mbar_wait(&empty[s1], (uint32_t)((c - 1) / S) & 1u, kWaitLimitNs)) { ok = false; break; }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&mdone[s]);
+      const int wn = w - 1 + S;  // refill the stage item w-1 used
+      if (w >= 1 && wn < n_work) {
+        const int s1 = (w - 1) % S;
+        if (!warp_wait(&done[s1], (uint32_t)((w - 1) / S) & 1u)) { ok = false; why |= 32; break; }
         if (lane == 0) {
           mbar_arrive_expect_tx(&full[s1], (uint32_t)L::STAGE_BYTES);
-          tma_load_3d(ks + s1 * align_up(L::STAGE_BYTES, 1024), &kmap, &full[s1], 0, cn * kN, b);
+          tma_load_3d(ks + s1 * L::STAGE_STRIDE, &kmap, &full[s1], 0, chunk_of(wn) * kN, b);
         }
       }
       __syncwarp();
     }
-    if (!ok && lane == 0) {
-      *abort_s = 1;
-      if (p.status) atomicOr(p.status, 2);
-    }
   } else {
-    // ------------------------------------------------------------ selection
-    const int r = threadIdx.x;  // row within the tile = TMEM lane
+    // ============================================================ selection
+    const int r = threadIdx.x;
     const bool row_ok = r < nrows;
     const int g = g0 + r;
-    float qf[R];
+    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
     float qabs = 0.f;
-    {
-      const TI* qrow = reinterpret_cast<const TI*>(p.q) + (int64_t)b * p.qsb + (int64_t)(l0 + (row_ok ? r : 0)) * p.qst;
+    if (row_ok) {
+      const TI* qrow = reinterpret_cast<const TI*>(p.q) + (int64_t)b * p.qsb + (int64_t)(l0 + r) * p.qst;
 #pragma unroll
       for (int c = 0; c < R / 8; ++c) {
         float f[8];
         Vec16<TI>::unpack(ldg16(qrow + c * 8), f);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          qf[c * 8 + e] = row_ok ? f[e] : 0.f;
-          qabs += fabsf(qf[c * 8 + e]);
-        }
+        for (int e = 0; e < 8; ++e) qabs += fabsf(f[e]);
       }
     }
-    uint32_t* mykey = bkey + r * L::KEY_STRIDE;
-    uint16_t* myidx = bidx + r * L::IDX_STRIDE;
-    int cnt = 0;
-    bool have_thr = false;
-    uint32_t thr_key = 0;
-    float thr_f = -INFINITY;
-    bool ok = true;
-    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    {
+      uint32_t ninf[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ninf[j] = 0xff800000u;
+#pragma unroll
+      for (int blk = 0; blk < kGroups / 32; ++blk) tmem_st_32x32b_x32(tmem_base + lane_base + 256 + blk * 32, ninf);
+      tmem_st_wait();
+    }
+    ok = warp_wait(qbar, 0);
+    if (!ok) why |= 64;
 
-    for (int c = 0; c < nchunks; ++c) {
-      const int s = c % S;
-      const uint32_t ph = (uint32_t)(c / S) & 1u;
-      if (!mbar_wait(&mdone[s], ph, kWaitLimitNs) || !mbar_wait(&full[s], ph, kWaitLimitNs)) { ok = false; break; }
+    // ---------------- pass 1: group maxima of tensor-core scores
+    for (int w = 0; w < n_own && ok; ++w) {
+      const int s = w % S;
+      if (!warp_wait(&mdone[s], (uint32_t)(w / S) & 1u)) { ok = false; why |= 128; break; }
       tc_fence_after();
-      const float eps = kEpsScale * qabs * kmax_s[s];
-      const float lim = have_thr ? thr_f - eps : -INFINITY;
-      const unsigned char* stage = ks + s * align_up(L::STAGE_BYTES, 1024);
+      const int c = chunk_of(w);
+      const uint32_t acc = tmem_base + lane_base + (uint32_t)((w & 1) * kN);
+      const uint32_t gcol = tmem_base + lane_base + 256 + (uint32_t)((w & 1) * kN);
 #pragma unroll 1
       for (int sl = 0; sl < kN / 32; ++sl) {
+        uint32_t v[32], gm[32];
+        tmem_ld_32x32b_x32(acc + sl * 32, v);
+        tmem_ld_32x32b_x32(gcol + sl * 32, gm);
+        tmem_ld_wait();
+        const int room = g - (c * kN + sl * 32);
+        if (row_ok && room >= 31) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) gm[j] = __float_as_uint(fmaxf(__uint_as_float(gm[j]), __uint_as_float(v[j])));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float x = (row_ok && j <= room) ? __uint_as_float(v[j]) : -INFINITY;
+            gm[j] = __float_as_uint(fmaxf(__uint_as_float(gm[j]), x));
+          }
+        }
+        tmem_st_32x32b_x32(gcol + sl * 32, gm);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&done[s]);
+    }
+
+    // ---------------- lower bound on the K-th best score from the group maxima
+    float theta_own = -INFINITY;
+    {
+      const uint32_t gbase = tmem_base + lane_base + 256;
+      int nf = 0;
+      float mn = INFINITY, mx = -INFINITY;
+#pragma unroll 1
+      for (int blk = 0; blk < kGroups / 32; ++blk) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_base + (uint32_t)(s * kN + sl * 32), v);
+        tmem_ld_32x32b_x32(gbase + blk * 32, v);
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          if (__uint_as_float(v[j]) >= lim) {
-            const int jj = sl * 32 + j;
-            const int key = c * kN + jj;
-            if (row_ok && key <= g) {
-              const float ex = rescore<TI>(qf, stage + jj * ROWB, jj, ROWB);
-              const uint32_t kk = ordered_key(ex);
-              if (!have_thr || kk > thr_key) {
-                mykey[cnt] = kk;
-                myidx[cnt] = (uint16_t)key;
-                ++cnt;
-              }
+          const float x = __uint_as_float(v[j]);
+          if (x > -INFINITY) {
+            ++nf;
+            mn = fminf(mn, x);
+            mx = fmaxf(mx, x);
+          }
+        }
+      }
+      // tcgen05.ld is warp-collective: every lane runs the bisection, only lanes
+      // with at least K finite maxima keep its result.
+      const bool bis = nf >= p.K;
+      if (__any_sync(kFullMask, bis)) {
+        // largest lo with #(maxima >= lo) >= K, to within (mx - mn) / 2^10
+        float lo = bis ? mn : 0.f, hi = bis ? mx : 0.f;
+#pragma unroll 1
+        for (int it = 0; it < 10; ++it) {
+          const float mid = lo + 0.5f * (hi - lo);
+          int c = 0;
+#pragma unroll 1
+          for (int blk = 0; blk < kGroups / 32; ++blk) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(gbase + blk * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) c += __uint_as_float(v[j]) >= mid ? 1 : 0;
+          }
+          if (c >= p.K) lo = mid;
+          else hi = mid;
+        }
+        if (bis) theta_own = lo;
+      }
+    }
+
+    // ---------------- exchange bounds and key magnitudes with the peer CTA
+    st_peer_u32(map_peer(&theta_in[r], peer), __float_as_uint(theta_own));
+    if (r == 0) st_peer_u32(map_peer(kmax_in_s, peer), *kmax_own_s);
+    mbar_arrive_peer(map_peer(xbar, peer));
+    if (!warp_wait_cluster(xbar, 0)) { ok = false; why |= 256; }
+    const float theta = fmaxf(theta_own, theta_in[r]);
+    const float kpair = fmaxf(__uint_as_float(*kmax_own_s), __uint_as_float(*kmax_in_s));
+    const float eps = kEpsScale * qabs * kpair;
+    float lim = theta > -INFINITY ? theta - eps : -INFINITY;
+
+    // ---------------- pass 2: admit, rescore exactly, keep candidates
+    uint32_t* queue = queues + warp * kQcap;
+    uint32_t* mykey = bkey + r * L::KEY_STRIDE;
+    int cnt = 0;
+    int qsize = 0;  // warp-uniform
+    const uint32_t ltmask = lanemask_lt();
+
+    auto flush = [&](const unsigned char* stage, int c) {
+      __syncwarp();
+      for (int e = lane; e < qsize; e += 32) {
+        const uint32_t ent = queue[e];
+        const int lr = ent & 31, jj = (ent >> 5) & 127, dest = (int)(ent >> 12);
+        const int row = 32 * warp + lr;
+        const float ex = dot_swizzled<TI, ROWB>(qs, row, stage, jj);
+        bkey[row * L::KEY_STRIDE + dest] = ordered_key(ex);
+        bidx[row * L::IDX_STRIDE + dest] = (uint16_t)(c * kN + jj);
+      }
+      __syncwarp();
+      qsize = 0;
+    };
+
+    for (int w = n_own; w < n_work && ok; ++w) {
+      const int s = w % S;
+      const uint32_t ph = (uint32_t)(w / S) & 1u;
+      if (!warp_wait(&mdone[s], ph) || !warp_wait(&full[s], ph)) { ok = false; why |= 512; break; }
+      tc_fence_after();
+      const int c = chunk_of(w);
+      const unsigned char* stage = ks + s * L::STAGE_STRIDE;
+      const uint32_t acc = tmem_base + lane_base + (uint32_t)((w & 1) * kN);
+#pragma unroll 1
+      for (int sl = 0; sl < kN / 32; ++sl) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(acc + sl * 32, v);
+        tmem_ld_wait();
+        uint32_t m = 0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) m |= (__uint_as_float(v[j]) >= lim ? 1u : 0u) << j;
+        const int room = g - (c * kN + sl * 32);
+        if (!row_ok || room < 0) m = 0;
+        else if (room < 31) m &= (2u << room) - 1u;
+        int np = __popc(m);
+        // rows whose buffer would overflow: rescore what is pending, then compact them
+        unsigned need = __ballot_sync(kFullMask, cnt + np > CAP);
+        if (need) {
+          flush(stage, c);
+          while (need) {
+            const int ln = __ffs(need) - 1;
+            need &= need - 1;
+            const int rr = 32 * warp + ln;
+            const int n = __shfl_sync(kFullMask, cnt, ln);
+            const uint32_t tau = merge_row<EPL>(bkey + rr * L::KEY_STRIDE, bidx + rr * L::IDX_STRIDE, n, p.K, lane);
+            if (lane == ln) {
+              cnt = p.K;
+              lim = fmaxf(lim, key_to_float(tau) - eps);
             }
           }
         }
-        unsigned need = __ballot_sync(kFullMask, cnt > CAP - 32);
-        while (need) {
-          const int ln = __ffs(need) - 1;
-          need &= need - 1;
-          const int rr = 32 * warp + ln;
-          const int n = __shfl_sync(kFullMask, cnt, ln);
-          const uint32_t tau = merge_row<EPL>(bkey + rr * L::KEY_STRIDE, bidx + rr * L::IDX_STRIDE, n, p.K, lane);
-          if (lane == ln) {
-            cnt = p.K;
-            thr_key = tau;
-            thr_f = key_to_float(tau);
-            have_thr = true;
-          }
+        // queue the admitted (row, key) pairs with their buffer slots
+        int incl = np;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int t = __shfl_up_sync(kFullMask, incl, o);
+          if (lane >= o) incl += t;
         }
+        const int total = __shfl_sync(kFullMask, incl, 31);
+        if (qsize + total > kQcap) flush(stage, c);
+        int pos = qsize + incl - np;
+        int k = 0;
+        while (m) {
+          const int j = __ffs(m) - 1;
+          m &= m - 1;
+          queue[pos + k] = (uint32_t)lane | ((uint32_t)(sl * 32 + j) << 5) | ((uint32_t)(cnt + k) << 12);
+          ++k;
+        }
+        cnt += np;
+        qsize += total;
+        (void)ltmask;
       }
+      flush(stage, c);  // the stage is about to be released
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if (lane == 0) mbar_arrive(&done[s]);
     }
-    if (!ok && lane == 0) {
-      *abort_s = 1;
-      if (p.status) atomicOr(p.status, 2);
-    }
+    (void)mykey;
 
-    // Finalise each row of this warp: exact top-K, sorted, pads.
-    for (int ln = 0; ln < 32; ++ln) {
-      const int rr = 32 * warp + ln;
+    // ---------------- own exact top-K per row, then publish to the peer
+    {
+      unsigned need = __ballot_sync(kFullMask, cnt > p.K);
+      while (need) {
+        const int ln = __ffs(need) - 1;
+        need &= need - 1;
+        const int rr = 32 * warp + ln;
+        const int n = __shfl_sync(kFullMask, cnt, ln);
+        merge_row<EPL>(bkey + rr * L::KEY_STRIDE, bidx + rr * L::IDX_STRIDE, n, p.K, lane);
+        if (lane == ln) cnt = p.K;
+      }
+    }
+    cnt_s[r] = cnt;
+    __syncwarp();
+    __threadfence();
+    // The final merge below reads rows other warps of this CTA built: sync the
+    // four selection warps (named barrier 1; the producer warp is not part of it).
+    asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+    mbar_arrive_peer(map_peer(rbar, peer));
+    if (!warp_wait_cluster(rbar, 0)) { ok = false; why |= 1024; }
+
+    // ---------------- merge own + peer candidates for rows [64 rank, 64 rank + 64)
+    for (int i = 0; i < 16; ++i) {
+      const int rr = 64 * (int)rank + 16 * warp + i;
       if (rr >= nrows) break;
-      int n = __shfl_sync(kFullMask, cnt, ln);
       uint32_t* bk = bkey + rr * L::KEY_STRIDE;
       uint16_t* bi = bidx + rr * L::IDX_STRIDE;
+      const int n1 = cnt_s[rr];
+      const int n2 = (int)ld_peer_u32(map_peer(&cnt_s[rr], peer));
+      const uint32_t pk = map_peer(bk, peer);
+      const uint32_t pi = map_peer(bi, peer);
+      uint32_t kk[EPLF];
+      int ii[EPLF];
+#pragma unroll
+      for (int t = 0; t < EPLF; ++t) {
+        const int e = t * 32 + lane;
+        if (e < n1) {
+          kk[t] = bk[e];
+          ii[t] = bi[e];
+        } else if (e < n1 + n2) {
+          kk[t] = ld_peer_u32(pk + 4 * (e - n1));
+          ii[t] = (int)ld_peer_u16(pi + 2 * (e - n1));
+        } else {
+          kk[t] = 0u;
+          ii[t] = INT_MAX;
+        }
+      }
+      __syncwarp();
+      int n = n1 + n2;
       if (n > p.K) {
-        merge_row<EPL>(bk, bi, n, p.K, lane);
+        select_compact<EPLF>(kk, ii, n, p.K, lane, bk, bi);
         n = p.K;
+      } else {
+#pragma unroll
+        for (int t = 0; t < EPLF; ++t) {
+          const int e = t * 32 + lane;
+          if (e < n) {
+            bk[e] = kk[t];
+            bi[e] = (uint16_t)ii[t];
+          }
+        }
+        __syncwarp();
       }
       uint64_t cc[SE];
 #pragma unroll
-      for (int i = 0; i < SE; ++i) {
-        const int e = i * 32 + lane;
-        cc[i] = (e < n) ? (((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e])) : 0ull;
+      for (int t = 0; t < SE; ++t) {
+        const int e = t * 32 + lane;
+        cc[t] = (e < n) ? (((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e])) : 0ull;
       }
       bitonic_sort_desc<SE>(cc, lane);
       const int gg = g0 + rr;
       int32_t* out = p.idx + ((int64_t)b * p.Tq + l0 + rr) * p.K;
 #pragma unroll
-      for (int i = 0; i < SE; ++i) {
-        const int s = i * 32 + lane;
+      for (int t = 0; t < SE; ++t) {
+        const int s = t * 32 + lane;
         if (s < p.K) {
           int val;
-          if (s < n) val = (int)(~(uint32_t)cc[i]);
+          if (s < n) val = (int)(~(uint32_t)cc[t]);
           else val = p.pad_mode == 0 ? (int)(((int64_t)gg + p.K + s + 1) % p.Tk) : -1;
           out[s] = val;
         }
       }
+      __syncwarp();
     }
+    __syncwarp();
+    mbar_arrive_peer(map_peer(dbar, peer));
+    if (!warp_wait_cluster(dbar, 0)) { ok = false; why |= 2048; }
   }
+  if (!ok && p.status) atomicOr(p.status, 2 | (int)why);
 
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // neither CTA leaves while its peer may still touch its shared memory
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
@@ -367,7 +592,7 @@ bool make_map(CUtensorMap* map, const void* ptr, bool bf16, int R, int64_t T, in
   const cuuint64_t strides[2] = {(cuuint64_t)(st * 2), (cuuint64_t)(sb * 2)};
   const cuuint32_t box[3] = {(cuuint32_t)R, (cuuint32_t)box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
-  const CUtensorMapSwizzle sw = R == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+  const CUtensorMapSwizzle sw = R == 64   ? CU_TENSOR_MAP_SWIZZLE_128B
                                 : R == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
                                           : CU_TENSOR_MAP_SWIZZLE_32B;
   CUresult rc = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
@@ -376,10 +601,29 @@ bool make_map(CUtensorMap* map, const void* ptr, bool bf16, int R, int64_t T, in
   return rc == CUDA_SUCCESS;
 }
 
-template <typename TI, int R, int EPL, int SE>
+// (EPL, SE, EPLF) per K class: buffer capacity 32*EPL >= K + 64, sort width 32*SE >= K, merge width 32*EPLF >= 2K.
+template <int R>
+size_t smem_for_k(int K) {
+  if (K <= 32) return Layout<R, 4>::smem;
+  if (K <= 64) return Layout<R, 5>::smem;
+  if (K <= 128) return Layout<R, 7>::smem;
+  return 0;
+}
+
+size_t tc_smem(int R, int K) {
+  switch (R) {
+    case 16: return smem_for_k<16>(K);
+    case 32: return smem_for_k<32>(K);
+    case 64: return smem_for_k<64>(K);
+    default: return 0;
+  }
+}
+
+template <typename TI, int R, int EPL, int SE, int EPLF>
 int launch_t(const TopkParams& p, cudaStream_t stream) {
   using L = Layout<R, EPL>;
-  auto kern = causal_topk_tc_kernel<TI, R, EPL, SE>;
+  if (L::smem > kMaxSmem) return -1;
+  auto kern = causal_topk_tc_kernel<TI, R, EPL, SE, EPLF>;
   static bool configured[kMaxDevices] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -402,16 +646,29 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
   t.rt = p.rt; t.rs = p.rs; t.r0 = p.r0;
   t.idx = p.idx;
   t.status = p.status;
-  dim3 grid((p.Tq + kM - 1) / kM, p.B);
-  kern<<<grid, kThreads, L::smem, stream>>>(qmap, kmap, t);
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * ((p.Tq + kM - 1) / kM), p.B);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, qmap, kmap, t);
+  if (e != cudaSuccess) return (int)e;
   return (int)cudaGetLastError();
 }
 
 template <typename TI, int R>
 int launch_r(const TopkParams& p, cudaStream_t s) {
-  if (p.K <= 32) return launch_t<TI, R, 4, 1>(p, s);
-  if (p.K <= 64) return launch_t<TI, R, 5, 2>(p, s);
-  if (p.K <= 128) return launch_t<TI, R, 7, 4>(p, s);
+  if (p.K <= 32) return launch_t<TI, R, 4, 1, 2>(p, s);
+  if (p.K <= 64) return launch_t<TI, R, 5, 2, 4>(p, s);
+  if (p.K <= 128) return launch_t<TI, R, 7, 4, 8>(p, s);
   return -1;
 }
 
@@ -431,6 +688,8 @@ bool topk_tc_supported(const TopkParams& p, int dtype) {
   if (dtype != kBF16 && dtype != kF16) return false;
   if (p.R != 16 && p.R != 32 && p.R != 64) return false;
   if (p.K > 128 || p.Tk > 65536 || p.B > 65535) return false;
+  const size_t sm = tc_smem(p.R, p.K);
+  if (sm == 0 || sm > kMaxSmem) return false;
   if (p.qsr != 1 || p.ksr != 1) return false;
   if ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.k)) % 16) return false;
   if ((p.qst * 2) % 16 || (p.kst * 2) % 16 || (p.qsb * 2) % 16 || (p.ksb * 2) % 16) return false;
@@ -446,3 +705,4 @@ int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream) {
 }
 
 }  // namespace wf
+
