@@ -177,6 +177,11 @@ int wf_sparse_attention(const void* q, const void* k, const void* v, int32_t dty
   p.scale = scale;
   p.mask_negative = (flags & WF_ATTN_MASK_NEGATIVE) ? 1 : 0;
   p.status = status;
+  {
+    const int osz = dtype_size(out_dtype);
+    p.out_vec_ok = (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (out_strides[0] * osz) % 16 == 0 &&
+                   (out_strides[1] * osz) % 16 == 0 && (out_strides[2] * osz) % 16 == 0;
+  }
   rc = wf::launch_sparse_attention(p, dtype, out_dtype, static_cast<cudaStream_t>(stream));
   if (rc) return cuda_fail(rc, "wf_sparse_attention");
   return ok();

@@ -8,13 +8,20 @@
 // computed in fp32 and rounded once to the output type.  Nothing of shape
 // (B,H,T,K,D) is materialised (the reference gathers it at :64-77).
 //
-// Design: one warp per (b, t, h); warps of a CTA share (b, t) so the index row
-// is read once into L1.  A K or V row of D elements is split across G lanes,
-// each loading 16-byte vectors, so 32/G retrieved rows are in flight per warp
-// instruction and every 32-byte sector fetched is fully used.  Phase 1 forms
-// the K scores (partial dot products reduced by xor-shuffles) into shared
-// memory, phase 2 is an exact two-pass softmax over the K scores, phase 3
-// accumulates p * v in fp32 registers and reduces across lane groups.
+// Design.  Indices are shared by the heads, so one warp serves one query and a
+// group of heads: each lane owns E consecutive elements (16-byte vectors) of one
+// head's row, L = D/E lanes cover a head and 32/L heads share the warp.  For
+// every retrieved key the index and row address are computed once for all those
+// heads, and the K and V rows of all of them are read with coalesced 16-byte
+// loads (lane `sub` of a head owns vectors sub, sub+L, ... so each load
+// instruction covers whole sectors) (in the module's (B,T,H,D) layout the heads of one key are contiguous).
+//   phase 1: partial dot products over the lane's E elements, reduced over the
+//            L lanes of the head by xor-shuffles; one score per (head, key) to
+//            shared memory;
+//   phase 2: exact two-pass softmax per head (max-subtracted, like F.softmax);
+//   phase 3: acc[E] += p * v in fp32 registers; the lane already owns its output
+//            elements, so no cross-lane reduction is needed.
+// The loop over keys is the same for K and V; a lane keeps U rows in flight.
 #include "wf_common.cuh"
 #include "wf_kernels.h"
 
@@ -23,47 +30,68 @@
 namespace wf {
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
 constexpr unsigned kFull = 0xffffffffu;
-constexpr int kUnroll = 8;  // retrieved rows in flight per lane
+constexpr int kU = 4;  // retrieved rows in flight per lane
 
 // Index slot states after decoding.
-constexpr int kMasked = -1;   // pad slot that is excluded from the softmax
-constexpr int kBad = -2;      // out-of-range index: output becomes NaN
+constexpr int kMasked = -1;  // pad slot that is excluded from the softmax
+constexpr int kBad = -2;     // out-of-range index: output becomes NaN
 
 template <typename TO>
-__device__ __forceinline__ void store_out(TO* o, const float* v, int n) {
+__device__ __forceinline__ void store_vec(TO* o, const float* v, int n) {
 #pragma unroll
   for (int i = 0; i < n; ++i) o[i] = from_f32<TO>(v[i]);
 }
+template <>
+__device__ __forceinline__ void store_vec<__nv_bfloat16>(__nv_bfloat16* o, const float* v, int n) {
+  for (int i = 0; i < n; i += 8) {
+    uint4 w;
+    uint32_t* u = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[i + 2 * e], v[i + 2 * e + 1]);
+      u[e] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(o + i) = w;
+  }
+}
+template <>
+__device__ __forceinline__ void store_vec<float>(float* o, const float* v, int n) {
+  for (int i = 0; i < n; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+}
 
-template <typename TI, typename TO, int D>
-__global__ void __launch_bounds__(kThreads) sparse_attn_kernel(const AttnParams p) {
+template <typename TI, typename TO, int D, int E>
+__global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, int warps_per_block) {
   using V16 = Vec16<TI>;
-  constexpr int VEC = V16::N;                 // elements per 16-byte vector
-  constexpr int NVROW = D / VEC;              // vectors per row
-  constexpr int G = NVROW < 32 ? NVROW : 32;  // lanes per retrieved row
-  constexpr int NV = NVROW / G;               // vectors per lane
-  constexpr int KPP = 32 / G;                 // rows per pass
-  constexpr int NE = NV * VEC;                // elements per lane
+  constexpr int VEC = V16::N;
+  constexpr int NV = E / VEC;       // 16-byte vectors per lane and row
+  constexpr int L = D / E;          // lanes per head
+  constexpr int HW = 32 / L;        // heads per warp
 
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* sS = reinterpret_cast<float*>(smem_raw) + (size_t)warp * 2 * p.K;
-  int* sI = reinterpret_cast<int*>(sS + p.K);
+  const int K = p.K;
+  const int KP = K | 1;  // odd row stride: the heads' score rows fall in different banks
+  int* sI = reinterpret_cast<int*>(smem_raw) + (size_t)warp * (K + HW * KP);
+  float* sP = reinterpret_cast<float*>(sI + K);  // [HW][KP]
 
-  const int64_t w = (int64_t)blockIdx.x * kWarps + warp;
-  if (w >= (int64_t)p.B * p.Tq * p.H) return;
-  const int h = (int)(w % p.H);
-  const int64_t bt = w / p.H;
+  const int ngroups = (p.H + HW - 1) / HW;
+  const int64_t w = (int64_t)blockIdx.x * warps_per_block + warp;
+  if (w >= (int64_t)p.B * p.Tq * ngroups) return;
+  const int hg = (int)(w % ngroups);
+  const int64_t bt = w / ngroups;
   const int t = (int)(bt % p.Tq);
   const int b = (int)(bt / p.Tq);
+  const int hl = lane / L;        // head within the warp
+  const int sub = lane % L;
+  const int h = hg * HW + hl;
+  const bool hv = h < p.H;
+  const int hc = hv ? h : 0;      // clamp for address arithmetic of idle lanes
 
-  // Decode the index row.
+  // Decode the index row once for all heads.
   const int32_t* ip = p.idx + (int64_t)b * p.isb + (int64_t)t * p.ist;
   bool bad = false;
-  for (int s = lane; s < p.K; s += 32) {
+  for (int s = lane; s < K; s += 32) {
     int j = ip[(int64_t)s * p.iss];
     if (j < 0) {
       if (p.mask_negative) j = kMasked;
@@ -77,36 +105,36 @@ __global__ void __launch_bounds__(kThreads) sparse_attn_kernel(const AttnParams 
   }
   if (__any_sync(kFull, bad) && lane == 0 && p.status) atomicOr(p.status, 1);
 
-  const int sub = lane % G, grp = lane / G;
-  float qf[NE];
+  float qf[E];
   {
-    const TI* qp = reinterpret_cast<const TI*>(p.q) + (int64_t)b * p.qsb + (int64_t)h * p.qsh +
+    const TI* qp = reinterpret_cast<const TI*>(p.q) + (int64_t)b * p.qsb + (int64_t)hc * p.qsh +
                    (int64_t)t * p.qst;
 #pragma unroll
-    for (int v = 0; v < NV; ++v) V16::unpack(ldg16(qp + (sub * NV + v) * VEC), qf + v * VEC);
+    for (int v = 0; v < NV; ++v) V16::unpack(ldg16(qp + (v * L + sub) * VEC), qf + v * VEC);
   }
   __syncwarp();
 
-  const TI* kbase = reinterpret_cast<const TI*>(p.k) + (int64_t)b * p.ksb + (int64_t)h * p.ksh;
-  const TI* vbase = reinterpret_cast<const TI*>(p.v) + (int64_t)b * p.vsb + (int64_t)h * p.vsh;
-  const int npass = (p.K + KPP - 1) / KPP;
+  // Lane `sub` of a head owns vectors sub, sub + L, ... of the row, so one load
+  // instruction reads whole 32-byte sectors.
+  const TI* kb = reinterpret_cast<const TI*>(p.k) + (int64_t)b * p.ksb + (int64_t)hc * p.ksh + sub * VEC;
+  const TI* vb = reinterpret_cast<const TI*>(p.v) + (int64_t)b * p.vsb + (int64_t)hc * p.vsh + sub * VEC;
+  float* myP = sP + hl * KP;
 
   // Phase 1: scores.
 #pragma unroll 1
-  for (int ps = 0; ps < npass; ps += kUnroll) {
-    uint4 raw[kUnroll][NV];
-    int jj[kUnroll];
+  for (int k0 = 0; k0 < K; k0 += kU) {
+    uint4 raw[kU][NV];
+    int jj[kU];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int slot = (ps + u) * KPP + grp;
-      const int j = (ps + u < npass && slot < p.K) ? sI[slot] : kMasked;
+    for (int u = 0; u < kU; ++u) {
+      const int j = (k0 + u < K) ? sI[k0 + u] : kMasked;
       jj[u] = j;
 #pragma unroll
       for (int v = 0; v < NV; ++v)
-        raw[u][v] = j >= 0 ? ldg16(kbase + (int64_t)j * p.kst + (sub * NV + v) * VEC) : make_uint4(0, 0, 0, 0);
+        raw[u][v] = (j >= 0 && hv) ? ldg16(kb + (int64_t)j * p.kst + v * L * VEC) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
       float d = 0.f;
 #pragma unroll
       for (int v = 0; v < NV; ++v) {
@@ -116,51 +144,51 @@ __global__ void __launch_bounds__(kThreads) sparse_attn_kernel(const AttnParams 
         for (int e = 0; e < VEC; ++e) d = fmaf(qf[v * VEC + e], kf[e], d);
       }
 #pragma unroll
-      for (int o = G / 2; o > 0; o >>= 1) d += __shfl_xor_sync(kFull, d, o);
-      const int slot = (ps + u) * KPP + grp;
-      if (sub == 0 && ps + u < npass && slot < p.K) {
+      for (int o = L / 2; o > 0; o >>= 1) d += __shfl_xor_sync(kFull, d, o);
+      if (sub == 0 && k0 + u < K) {
         const int j = jj[u];
-        sS[slot] = j >= 0 ? d * p.scale : (j == kMasked ? -INFINITY : NAN);
+        myP[k0 + u] = j >= 0 ? d * p.scale : (j == kMasked ? -INFINITY : NAN);
       }
     }
   }
   __syncwarp();
 
-  // Phase 2: softmax over the K scores (max-subtracted, like F.softmax).
+  // Phase 2: softmax of each head over its K scores; the L lanes of a head share the work.
   float m = -INFINITY;
-  for (int s = lane; s < p.K; s += 32) m = fmaxf(m, sS[s]);
-  m = warp_max(m);
+  for (int s = sub; s < K; s += L) m = fmaxf(m, myP[s]);
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
   float sum = 0.f;
-  for (int s = lane; s < p.K; s += 32) {
-    const float x = sS[s];
+  for (int s = sub; s < K; s += L) {
+    const float x = myP[s];
     const float e = (x == -INFINITY) ? 0.f : expf(x - m);
-    sS[s] = e;
+    myP[s] = e;
     sum += e;
   }
-  sum = warp_sum(sum);
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(kFull, sum, o);
   __syncwarp();
   const float inv = 1.0f / sum;
 
-  // Phase 3: out = sum_k p_k v_k.
-  float acc[NE];
+  // Phase 3: out = sum_k p_k v_k over the lane's own E elements.
+  float acc[E];
 #pragma unroll
-  for (int e = 0; e < NE; ++e) acc[e] = 0.f;
+  for (int e = 0; e < E; ++e) acc[e] = 0.f;
 #pragma unroll 1
-  for (int ps = 0; ps < npass; ps += kUnroll) {
-    uint4 raw[kUnroll][NV];
-    float pw[kUnroll];
+  for (int k0 = 0; k0 < K; k0 += kU) {
+    uint4 raw[kU][NV];
+    float pw[kU];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int slot = (ps + u) * KPP + grp;
-      const bool in = ps + u < npass && slot < p.K;
-      const int j = in ? sI[slot] : kMasked;
-      pw[u] = in ? sS[slot] : 0.f;
+    for (int u = 0; u < kU; ++u) {
+      const bool in = k0 + u < K;
+      const int j = in ? sI[k0 + u] : kMasked;
+      pw[u] = in ? myP[k0 + u] : 0.f;
 #pragma unroll
       for (int v = 0; v < NV; ++v)
-        raw[u][v] = j >= 0 ? ldg16(vbase + (int64_t)j * p.vst + (sub * NV + v) * VEC) : make_uint4(0, 0, 0, 0);
+        raw[u][v] = (j >= 0 && hv) ? ldg16(vb + (int64_t)j * p.vst + v * L * VEC) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
 #pragma unroll
       for (int v = 0; v < NV; ++v) {
         float vf[VEC];
@@ -170,37 +198,65 @@ __global__ void __launch_bounds__(kThreads) sparse_attn_kernel(const AttnParams 
       }
     }
   }
+  if (hv) {
 #pragma unroll
-  for (int o = G; o < 32; o <<= 1)
-#pragma unroll
-    for (int e = 0; e < NE; ++e) acc[e] += __shfl_xor_sync(kFull, acc[e], o);
-
-  if (grp == 0) {
-#pragma unroll
-    for (int e = 0; e < NE; ++e) acc[e] *= inv;
+    for (int e = 0; e < E; ++e) acc[e] *= inv;
     TO* op = reinterpret_cast<TO*>(p.out) + (int64_t)b * p.osb + (int64_t)h * p.osh + (int64_t)t * p.ost;
 #pragma unroll
-    for (int v = 0; v < NV; ++v) store_out<TO>(op + (sub * NV + v) * VEC, acc + v * VEC, VEC);
+    for (int v = 0; v < NV; ++v) {
+      TO* o = op + (v * L + sub) * VEC;
+      if (p.out_vec_ok) store_vec<TO>(o, acc + v * VEC, VEC);
+      else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] = from_f32<TO>(acc[v * VEC + e]);
+      }
+    }
   }
 }
 
-template <typename TI, typename TO, int D>
+constexpr size_t kSmemBudget = 96 * 1024;
+
+template <typename TI, typename TO, int D, int E>
 int launch_t(const AttnParams& p, cudaStream_t stream) {
-  const int64_t work = (int64_t)p.B * p.Tq * p.H;
-  const int64_t blocks = (work + kWarps - 1) / kWarps;
-  const size_t smem = (size_t)kWarps * 2 * p.K * sizeof(float);
-  sparse_attn_kernel<TI, TO, D><<<(unsigned)blocks, kThreads, smem, stream>>>(p);
+  constexpr int L = D / E;
+  constexpr int HW = 32 / L;
+  const int ngroups = (p.H + HW - 1) / HW;
+  const size_t per_warp = ((size_t)p.K + (size_t)HW * (p.K | 1)) * sizeof(int);
+  int wpb = (int)(kSmemBudget / per_warp);
+  wpb = wpb < 1 ? 1 : (wpb > 8 ? 8 : wpb);
+  const size_t smem = per_warp * wpb;
+  auto kern = sparse_attn_kernel<TI, TO, D, E>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+  }
+  const int64_t work = (int64_t)p.B * p.Tq * ngroups;
+  const int64_t blocks = (work + wpb - 1) / wpb;
+  kern<<<(unsigned)blocks, wpb * 32, smem, stream>>>(p, wpb);
   return (int)cudaGetLastError();
+}
+
+// E: elements per lane.  16 when the heads of a query span at least 512
+// elements (every lane busy), else 8; never more than D.
+template <typename TI, typename TO, int D>
+int launch_e(const AttnParams& p, cudaStream_t s) {
+  constexpr int EMIN = 16 / sizeof(TI);  // one 16-byte vector
+  constexpr int E16 = D < 16 ? D : 16;
+  constexpr int E8 = D < 8 ? D : 8;
+  constexpr int EA = E16 < EMIN ? EMIN : E16;
+  constexpr int EB = E8 < EMIN ? EMIN : E8;
+  if ((int64_t)p.H * D >= 32 * EA) return launch_t<TI, TO, D, EA>(p, s);
+  return launch_t<TI, TO, D, EB>(p, s);
 }
 
 template <typename TI, typename TO>
 int launch_d(const AttnParams& p, cudaStream_t s) {
   switch (p.D) {
-    case 16: return launch_t<TI, TO, 16>(p, s);
-    case 32: return launch_t<TI, TO, 32>(p, s);
-    case 64: return launch_t<TI, TO, 64>(p, s);
-    case 128: return launch_t<TI, TO, 128>(p, s);
-    case 256: return launch_t<TI, TO, 256>(p, s);
+    case 16: return launch_e<TI, TO, 16>(p, s);
+    case 32: return launch_e<TI, TO, 32>(p, s);
+    case 64: return launch_e<TI, TO, 64>(p, s);
+    case 128: return launch_e<TI, TO, 128>(p, s);
+    case 256: return launch_e<TI, TO, 256>(p, s);
     default: return -1;
   }
 }

@@ -40,6 +40,7 @@ struct AttnParams {
   int B, H, Tq, Tk, D, K;
   float scale;
   int mask_negative;     // 1: negative index = masked slot; 0: wraps like torch indexing
+  int out_vec_ok;        // output rows are 16-byte aligned (vector stores allowed)
   int32_t* status;       // nullable; bit 0 set on an out-of-range index
 };
 
