@@ -41,6 +41,9 @@ from wayfinder_attention_b200.workloads import CONFIGS, Workload, make_inputs, s
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 << 20
 METRIC = "fused top-K+sparse-attn fwd queries/s @T=16K,K=128"
+# dram__bytes_read.sum + dram__bytes_write.sum of one sparse-attention launch, from the
+# ncu capture summarised in profiles/sparse_attention_cfg2.md (58.0 MB + 4.4 MB).
+ATTN_DRAM_BYTES = {"cfg2": 62.3e6}
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -309,7 +312,8 @@ def main() -> None:
             "query_heads_per_s": value * w.H,
             "kernels_ms": {"causal_topk": topk_ms_launch, "sparse_attention": attn_ms_launch},
             "roofline": {"kernel": "sparse_attention", "bound": "hbm", "achieved": achieved_gbs, "peak": hbm,
-                         "unit": "GB/s", "frac": achieved_gbs / hbm, "traffic": None,
+                         "unit": "GB/s", "frac": achieved_gbs / hbm,
+                         "traffic": ATTN_DRAM_BYTES.get(w.name),
                          "peak_kind": peak_kind,
                          "note": "achieved = gathered K/V bytes (2*B*H*T*K*D*2) / kernel time; K/V fit in L2"},
             "path_roofline": {"roofline_ms": roof_s * 1e3, "frac": roof_s * 1e3 / ms_per_step,
