@@ -208,6 +208,12 @@ def main() -> None:
         if world > 1:
             dist.barrier()
 
+    if args.config == "cfg4" and world > 1:
+        run_sequence_sharded(args, w, rank, world, dev)
+        dist.barrier()
+        dist.destroy_process_group()
+        return
+
     # batch sharding: each rank owns batch element(s) `rank` of a global batch of world * B
     w_local = scaled(w, B=w.B)
     host = make_inputs(w_local, batch_offset=rank)
@@ -340,6 +346,64 @@ def main() -> None:
         dist.destroy_process_group()
     if result is not None:
         print(json.dumps(result), flush=True)
+
+
+def run_sequence_sharded(args, w: Workload, rank: int, world: int, dev) -> None:
+    """cfg4: one T=65536 sequence, query-row blocks over ranks, address and K/V all-gathers (strong scaling)."""
+    import torch.distributed as dist
+
+    from wayfinder_attention_b200.sharding import SequenceShardedAttention, local_rows
+
+    tile = 256
+    if w.T % (world * tile):
+        raise SystemExit(f"T={w.T} is not a multiple of world*tile={world * tile}")
+    g = torch.Generator(device=dev).manual_seed(45)  # identical full inputs on every rank
+    qa = (torch.randn(w.B, w.T, w.R, generator=g, device=dev) / 32 ** 0.5).to(w.dtype)
+    ka = (torch.randn(w.B, w.T, w.R, generator=g, device=dev) / 32 ** 0.5).to(w.dtype)
+    qkv = [torch.randn(w.B, w.T, w.H, w.D, generator=g, device=dev).to(w.dtype) for _ in range(3)]
+    rows = torch.from_numpy(local_rows(w.T, world, rank, tile)).to(dev)
+    qa_l, ka_l = qa[:, rows].contiguous(), ka[:, rows].contiguous()
+    q_l, k_l, v_l = (t[:, rows].contiguous().transpose(1, 2) for t in qkv)
+    del qa, ka, qkv
+    op = SequenceShardedAttention(w.K, w.D ** -0.5, tile=tile)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        flush.zero_()
+        op(qa_l, ka_l, q_l, k_l, v_l)
+    torch.cuda.synchronize()
+    dist.barrier()
+    stream = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    dist.barrier()
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", 0))) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            dist.barrier()  # all ranks enter the step together, outside the timed events
+            ev[i][0].record(stream)
+            op(qa_l, ka_l, q_l, k_l, v_l)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    dist.barrier()
+    tot = torch.tensor([sum(a.elapsed_time(b) for a, b in ev)], dtype=torch.float64, device=dev)
+    dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    ms = tot.item() / args.steps
+    if rank == 0:
+        peaks, peak_kind = load_peaks()
+        roof_ms = 1e3 * max(w.score_flops() / (float(peaks["bf16_tflops"]) * 1e12),
+                            w.gathered_bytes() / (float(peaks["hbm_gbs"]) * 1e9)) / world
+        print(json.dumps({
+            "metric": METRIC, "value": w.B * w.T / (ms / 1e3), "unit": "queries/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, generated on device)",
+            "config": {"workload": w.name, "B": w.B, "H": w.H, "T": w.T, "D": w.D, "d_A": w.R, "K": w.K,
+                       "parallelism": f"query-row blocks of {tile} cyclic over {world} ranks; "
+                                      "k_addr and K/V all-gathered with NCCL",
+                       "l2": "flushed before every timed step"},
+            "path_roofline": {"roofline_ms_per_gpu": roof_ms, "frac": roof_ms / ms, "peak_kind": peak_kind},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }), flush=True)
 
 
 def dense_baseline(w: Workload, x: dict, flush: torch.Tensor, steps: int) -> dict:

@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the kernels use:
-// mbarriers, TMA tile loads (no multicast), and tcgen05 (TMEM alloc, MMA,
+// mbarriers, TMA tile loads into this CTA only, and tcgen05 (TMEM alloc, MMA,
 // commit, loads, fences).  Every wait is bounded by a wall-clock limit so a
 // lost arrival turns into an error flag instead of a hung GPU.
 #pragma once

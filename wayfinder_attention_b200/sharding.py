@@ -58,3 +58,90 @@ def sharded_causal_topk(q_addr_local: torch.Tensor, k_addr_full: torch.Tensor, t
         raise ValueError(f"rank {rank} of {world} owns {expect} rows at tile={tile}, got {q_addr_local.shape[1]}")
     q, k, _ = promote_compute_dtype(q_addr_local, k_addr_full)
     return _launch_topk(q, k, top_k, pad_mode, row_tile=tile, row_stride=world, row_start=rank)
+
+
+def _all_gather_rows(x_local: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """All-gather (B, Tl, ...) shards along dim 1 into a rank-major (world, B, Tl, ...) tensor."""
+    import torch.distributed as dist
+
+    x_local = x_local.contiguous()
+    out = torch.empty((world,) + tuple(x_local.shape), dtype=x_local.dtype, device=x_local.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, x_local, group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), x_local, group=group)
+    return out
+
+
+def gather_sequence(x_local: torch.Tensor, tile: int, group=None) -> torch.Tensor:
+    """Rebuild the full sequence from cyclic row-block shards.
+
+    x_local: (B, Tl, ...) holding this rank's rows ``local_rows(T, world, rank, tile)`` in order.
+    Returns (B, T, ...) in global row order.  Requires T = world * Tl with Tl a multiple of
+    ``tile`` (every rank holds the same number of whole blocks).  One all-gather
+    (NCCL over NVLink on GPUs, any backend elsewhere) plus one reordering copy.
+    """
+    import torch.distributed as dist
+
+    B, Tl = x_local.shape[0], x_local.shape[1]
+    if Tl % tile:
+        raise ValueError(f"local rows {Tl} are not a whole number of {tile}-row blocks")
+    world = dist.get_world_size(group)
+    g = _all_gather_rows(x_local, world, group)  # (W, B, Tl, ...)
+    nblk = Tl // tile
+    rest = tuple(x_local.shape[2:])
+    g = g.view((world, B, nblk, tile) + rest)
+    # global block index = local block * world + rank
+    g = g.permute((1, 2, 0, 3) + tuple(range(4, 4 + len(rest))))
+    return g.reshape((B, world * Tl) + rest)
+
+
+class SequenceShardedAttention:
+    """Fused retrieval + sparse attention for ONE long sequence split over ranks.
+
+    Rank r holds the query rows ``local_rows(T, W, r, tile)`` of the addresses and of
+    q/k/v (in the module's (B, T, H, D) memory layout).  Every rank needs all key
+    addresses and every K/V row up to its last query, so ``forward``:
+      1. all-gathers the key addresses (B*T*d_A elements, small) and starts the
+         K/V all-gather on a side stream;
+      2. runs the causal top-K of its own rows against all keys (row map of
+         ``wf_causal_topk``) while K/V are in flight;
+      3. waits for K/V and runs the sparse attention of its rows.
+    The only collectives are these all-gathers; nothing crosses ranks afterwards.
+    """
+
+    def __init__(self, top_k: int, scale: float, tile: int = 256, group=None, pad_mode: str = "reference"):
+        self.top_k = top_k
+        self.scale = scale
+        self.tile = tile
+        self.group = group
+        self.pad_mode = pad_mode
+
+    def forward(self, q_addr_l: torch.Tensor, k_addr_l: torch.Tensor, q_l: torch.Tensor, k_l: torch.Tensor,
+                v_l: torch.Tensor, out_dtype: torch.dtype | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """q_addr_l, k_addr_l: (B, Tl, R); q_l, k_l, v_l: (B, H, Tl, D) views of (B, Tl, H, D) memory."""
+        import torch.distributed as dist
+
+        from .fused_sparse import _launch_attention
+
+        world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
+        B, H, Tl, D = q_l.shape
+        T = world * Tl
+        main = torch.cuda.current_stream(q_l.device)
+        side = torch.cuda.Stream(device=q_l.device)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            k_full = gather_sequence(k_l.transpose(1, 2), self.tile, self.group).transpose(1, 2)
+            v_full = gather_sequence(v_l.transpose(1, 2), self.tile, self.group).transpose(1, 2)
+        k_addr = gather_sequence(k_addr_l, self.tile, self.group)
+        idx = sharded_causal_topk(q_addr_l, k_addr, self.top_k, world, rank, self.tile, self.pad_mode)
+        main.wait_stream(side)
+        k_full.record_stream(main)
+        v_full.record_stream(main)
+        out = _launch_attention(q_l, k_full, v_full, idx, self.scale, mask_negative=self.pad_mode == "masked",
+                                out_dtype=out_dtype)
+        assert k_full.shape[2] == T
+        return out, idx
+
+    __call__ = forward
