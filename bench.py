@@ -59,56 +59,69 @@ def dist_env() -> tuple[int, int, int]:
 
 
 class ClockSampler:
-    """nvidia-smi sampler run during the timed region."""
+    """Samples SM clock and clock-event reasons during the timed region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    Reads NVML (read-only queries) every ~2 ms from a background thread, so even a
+    timed region of a few tens of milliseconds gets samples; falls back to an
+    `nvidia-smi` poll if NVML is unavailable.
+    """
+
+    REASONS = {
+        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4,
+        "hw_power_brake_slowdown": 0x80,
+    }
 
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
-        self.proc = None
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = False
+        self._thread = None
+
+    def _run(self):
+        import pynvml
+
+        h = None
+        try:  # map the CUDA device to NVML through its PCI address (CUDA_VISIBLE_DEVICES may renumber)
+            pr = torch.cuda.get_device_properties(self.gpu_index)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu_index)
+        self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        while not self._stop:
+            self.samples.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+            r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+            for name, bit in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+            time.sleep(0.002)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
-                 "-i", str(self.gpu_index)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            import threading
+
+            pynvml.nvmlInit()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+            time.sleep(0.005)  # first sample before the timed region starts
+        except Exception:
+            self._thread = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        self._stop = True
+        if self._thread is not None:
+            self._thread.join(timeout=2)
         return False
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 def cpu_model() -> str:
