@@ -15,6 +15,7 @@
 #ifndef WAYFINDER_H_
 #define WAYFINDER_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -74,13 +75,25 @@ WF_API int wf_max_top_k(void);
  *             query-row-sharded long sequence addresses its cyclic row blocks.
  *   idx_out : (B, Tq, K_eff) int32, contiguous.  Slots hold the retrieved key indices in
  *             descending score order; equal scores break to the lower index.
+ *   workspace, workspace_bytes: device scratch of at least wf_causal_topk_workspace_bytes();
+ *             may be NULL/0 when that returns 0.
  *   status  : optional device int32; bit 1 is OR-ed in if a bounded internal wait of the
  *             tensor-core kernel timed out (the output is then invalid).  May be NULL.
  */
 WF_API int wf_causal_topk(const void* q_addr, const void* k_addr, int32_t dtype, int64_t B, int64_t Tq,
                    int64_t Tk, int32_t R, const int64_t* q_strides, const int64_t* k_strides,
                    int32_t top_k, int32_t pad_mode, int32_t row_tile, int32_t row_stride,
-                   int32_t row_start, int32_t* idx_out, int32_t* status, void* stream);
+                   int32_t row_start, int32_t* idx_out, void* workspace, size_t workspace_bytes,
+                   int32_t* status, void* stream);
+
+/*
+ * Device workspace (bytes, 16-byte aligned) that wf_causal_topk and
+ * wf_fused_sparse_attention need for these sizes: the tensor-core retrieval
+ * kernel parks each row's exact candidates there (about 7 KB per query row at
+ * K = 128) for its finalisation pass.  0 means none is needed.
+ */
+WF_API size_t wf_causal_topk_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, int32_t R, int32_t top_k,
+                                             int32_t dtype);
 
 /*
  * Softmax attention over the K rows named by idx, shared by all heads.  Replaces
@@ -118,7 +131,8 @@ WF_API int wf_fused_sparse_attention(const void* q_addr, const void* k_addr, int
                               const int64_t* v_strides, int32_t top_k, float scale,
                               int32_t pad_mode, int32_t row_tile, int32_t row_stride,
                               int32_t row_start, int32_t* idx_out, void* out, int32_t out_dtype,
-                              const int64_t* out_strides, int32_t* status, void* stream);
+                              const int64_t* out_strides, void* workspace, size_t workspace_bytes,
+                              int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -42,15 +42,15 @@ def _i64(*v):
 def test_invalid_arguments_fail_without_gpu():
     lib = _lib.load_library()
     s = _i64(1, 1, 1)
-    rc = lib.wf_causal_topk(None, None, 0, 1, -5, 10, 32, s, s, 8, 0, 0, 1, 0, None, None, None)
+    rc = lib.wf_causal_topk(None, None, 0, 1, -5, 10, 32, s, s, 8, 0, 0, 1, 0, None, None, 0, None, None)
     assert rc == _lib.WF_ERR_INVALID_ARGUMENT
     assert b"negative" in lib.wf_last_error()
-    rc = lib.wf_causal_topk(None, None, 7, 1, 5, 10, 32, s, s, 8, 0, 0, 1, 0, None, None, None)
+    rc = lib.wf_causal_topk(None, None, 7, 1, 5, 10, 32, s, s, 8, 0, 0, 1, 0, None, None, 0, None, None)
     assert rc == _lib.WF_ERR_INVALID_ARGUMENT and b"dtype" in lib.wf_last_error()
-    rc = lib.wf_causal_topk(None, None, 0, 1, 5, 10, 32, s, s, 8, 9, 0, 1, 0, None, None, None)
+    rc = lib.wf_causal_topk(None, None, 0, 1, 5, 10, 32, s, s, 8, 9, 0, 1, 0, None, None, 0, None, None)
     assert rc == _lib.WF_ERR_INVALID_ARGUMENT and b"pad_mode" in lib.wf_last_error()
     # empty work is a successful no-op
-    rc = lib.wf_causal_topk(None, None, 0, 0, 5, 10, 32, s, s, 8, 0, 0, 1, 0, None, None, None)
+    rc = lib.wf_causal_topk(None, None, 0, 0, 5, 10, 32, s, s, 8, 0, 0, 1, 0, None, None, 0, None, None)
     assert rc == _lib.WF_OK
     s4 = _i64(1, 1, 1, 1)
     rc = lib.wf_sparse_attention(None, None, None, 0, None, 1, 1, 4, 4, 48, 4, s4, s4, s4, s, 1.0, 0, None, 0,
@@ -61,10 +61,10 @@ def test_invalid_arguments_fail_without_gpu():
     assert rc == _lib.WF_ERR_INVALID_ARGUMENT and b"scale" in lib.wf_last_error()
     # row map reaching beyond the keys
     rc = lib.wf_causal_topk(ctypes.c_void_p(16), ctypes.c_void_p(16), 0, 1, 128, 128, 32, s, s, 8, 0, 64, 2, 1,
-                            ctypes.c_void_p(16), None, None)
+                            ctypes.c_void_p(16), None, 0, None, None)
     assert rc == _lib.WF_ERR_INVALID_ARGUMENT and b"row map" in lib.wf_last_error()
     rc = lib.wf_causal_topk(ctypes.c_void_p(16), ctypes.c_void_p(16), 0, 1, 128, 4096, 32, s, s, 300, 0, 0, 1, 0,
-                            ctypes.c_void_p(16), None, None)
+                            ctypes.c_void_p(16), None, 0, None, None)
     assert rc == _lib.WF_ERR_UNSUPPORTED and b"maximum" in lib.wf_last_error()
 
 
@@ -129,3 +129,11 @@ def test_synthetic_inputs_are_seeded_and_laid_out_like_the_module():
         assert torch.equal(a[k], b[k])
     assert a["q"].shape == (1, 4, 2048, 64) and a["q"].transpose(1, 2).is_contiguous()
     assert abs(a["q_addr"].float().std().item() - 32 ** -0.5) < 0.01
+
+
+def test_workspace_query():
+    lib = _lib.load_library()
+    assert lib.wf_causal_topk_workspace_bytes(1, 16384, 16384, 32, 128, _lib.WF_DTYPE_BF16) == 16384 * (2 * 224 * 8 + 8)
+    assert lib.wf_causal_topk_workspace_bytes(2, 100, 100, 32, 64, _lib.WF_DTYPE_F16) == 200 * (2 * 160 * 8 + 8)
+    assert lib.wf_causal_topk_workspace_bytes(1, 2048, 2048, 32, 128, _lib.WF_DTYPE_F32) == 0  # CUDA-core path
+    assert lib.wf_causal_topk_workspace_bytes(1, 2048, 2048, 32, 256, _lib.WF_DTYPE_BF16) == 0

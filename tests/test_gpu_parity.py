@@ -364,3 +364,19 @@ def test_tensor_core_topk_equals_cuda_core(R, K, T, B, dtype, clustered, cuda_de
     assert status.item() == 0
     mism = (tc != cc).any(dim=-1)
     assert not mism.any(), f"{int(mism.sum())} rows differ, first {torch.nonzero(mism)[:5].tolist()}"
+
+
+def test_workspace_too_small_is_rejected(cuda_device):
+    import ctypes
+
+    from wayfinder_attention_b200 import _lib
+
+    w = Workload("t", 1, 1, 512, 16, 32, 64, torch.bfloat16)
+    x = to_device(make_inputs(w), cuda_device)
+    lib = _lib.load_library()
+    idx = torch.empty(1, 512, 64, dtype=torch.int32, device=cuda_device)
+    ws = torch.empty(1024, dtype=torch.uint8, device=cuda_device)
+    rc = lib.wf_causal_topk(x["q_addr"].data_ptr(), x["k_addr"].data_ptr(), _lib.WF_DTYPE_BF16, 1, 512, 512, 32,
+                            _lib.strides(x["q_addr"]), _lib.strides(x["k_addr"]), 64, 0, 0, 1, 0, idx.data_ptr(),
+                            ws.data_ptr(), ws.numel(), None, _lib.stream_ptr(cuda_device))
+    assert rc == _lib.WF_ERR_INVALID_ARGUMENT and b"workspace" in lib.wf_last_error()

@@ -13,7 +13,10 @@ from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "libwayfinder_sm100.so"
+import os
+
+# WF_LIB_PATH points at an alternative build of the same library (e.g. an instrumented one).
+LIB_PATH = Path(os.environ.get("WF_LIB_PATH") or Path(__file__).resolve().parent / "libwayfinder_sm100.so")
 
 WF_DTYPE_BF16 = 0
 WF_DTYPE_F16 = 1
@@ -32,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "wf_version",
     "wf_last_error",
     "wf_max_top_k",
+    "wf_causal_topk_workspace_bytes",
     "wf_causal_topk",
     "wf_sparse_attention",
     "wf_fused_sparse_attention",
@@ -62,8 +66,11 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.wf_max_top_k.argtypes = []
     lib.wf_causal_topk.restype = ctypes.c_int
     lib.wf_causal_topk.argtypes = [
-        _vp, _vp, _i32, _i64, _i64, _i64, _i32, _i64p, _i64p, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
+        _vp, _vp, _i32, _i64, _i64, _i64, _i32, _i64p, _i64p, _i32, _i32, _i32, _i32, _i32, _vp,
+        _vp, ctypes.c_size_t, _vp, _vp,
     ]
+    lib.wf_causal_topk_workspace_bytes.restype = ctypes.c_size_t
+    lib.wf_causal_topk_workspace_bytes.argtypes = [_i64, _i64, _i64, _i32, _i32, _i32]
     lib.wf_sparse_attention.restype = ctypes.c_int
     lib.wf_sparse_attention.argtypes = [
         _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i32, _i32,
@@ -74,7 +81,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         _vp, _vp, _i32, _i32, _i64p, _i64p,
         _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32,
         _i64p, _i64p, _i64p, _i32, _f32, _i32, _i32, _i32, _i32,
-        _vp, _vp, _i32, _i64p, _vp, _vp,
+        _vp, _vp, _i32, _i64p, _vp, ctypes.c_size_t, _vp, _vp,
     ]
 
 
@@ -116,6 +123,14 @@ def check(rc: int) -> None:
     if rc in (WF_ERR_INVALID_ARGUMENT, WF_ERR_UNSUPPORTED):
         raise ValueError(msg)
     raise RuntimeError(msg)
+
+
+def workspace(B: int, Tq: int, Tk: int, R: int, top_k: int, dtype: torch.dtype, device) -> torch.Tensor | None:
+    """Scratch the retrieval kernel needs (None if none), from torch's caching allocator."""
+    n = load_library().wf_causal_topk_workspace_bytes(B, Tq, Tk, R, top_k, dtype_code(dtype))
+    if n == 0:
+        return None
+    return torch.empty(n, dtype=torch.uint8, device=device)
 
 
 def stream_ptr(device: torch.device) -> int:

@@ -79,11 +79,13 @@ def _launch_topk(
         out = torch.empty(B, Tq, max(k_eff, 0), dtype=torch.int32, device=dev)
     elif out.dtype != torch.int32 or not out.is_contiguous() or tuple(out.shape) != (B, Tq, k_eff):
         raise ValueError(f"out must be a contiguous int32 tensor of shape {(B, Tq, k_eff)}")
+    ws = _lib.workspace(B, Tq, Tk, R, int(top_k), q.dtype, dev)
     with torch.cuda.device(dev):
         rc = lib.wf_causal_topk(
             q.data_ptr(), k.data_ptr(), _lib.dtype_code(q.dtype), B, Tq, Tk, R,
             _lib.strides(q), _lib.strides(k), int(top_k), pad_mode_code(pad_mode),
             int(row_tile), int(row_stride), int(row_start), out.data_ptr(),
+            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
             status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
         )
     _lib.check(rc)

@@ -28,6 +28,8 @@ int ok() {
 }
 
 int cuda_fail(int rc, const char* what) {
+  if (rc == -3) return fail(WF_ERR_INVALID_ARGUMENT, "%s: workspace missing, misaligned or too small "
+                            "(query wf_causal_topk_workspace_bytes)", what);
   if (rc < 0) return fail(WF_ERR_UNSUPPORTED, "%s: unsupported configuration", what);
   return fail(WF_ERR_CUDA, "%s: CUDA error %d (%s)", what, rc, cudaGetErrorString((cudaError_t)rc));
 }
@@ -133,10 +135,20 @@ const char* wf_last_error(void) { return g_err.c_str(); }
 
 int wf_max_top_k(void) { return wf::topk_max_k(); }
 
+size_t wf_causal_topk_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, int32_t R, int32_t top_k, int32_t dtype) {
+  if (B <= 0 || Tq <= 0 || Tk <= 0 || top_k <= 0) return 0;
+  const int64_t k_eff = top_k < Tk ? top_k : Tk;
+  if (dtype != WF_DTYPE_BF16 && dtype != WF_DTYPE_F16) return 0;
+  if (R != 16 && R != 32 && R != 64) return 0;
+  if (Tk > 65536) return 0;
+  return wf::topk_tc_workspace_bytes(B, Tq, (int)k_eff);
+}
+
 int wf_causal_topk(const void* q_addr, const void* k_addr, int32_t dtype, int64_t B, int64_t Tq,
                    int64_t Tk, int32_t R, const int64_t* q_strides, const int64_t* k_strides,
                    int32_t top_k, int32_t pad_mode, int32_t row_tile, int32_t row_stride,
-                   int32_t row_start, int32_t* idx_out, int32_t* status, void* stream) {
+                   int32_t row_start, int32_t* idx_out, void* workspace, size_t workspace_bytes,
+                   int32_t* status, void* stream) {
   int32_t k_eff = 0;
   int rc = check_topk(q_addr, k_addr, dtype, B, Tq, Tk, R, q_strides, k_strides, top_k, pad_mode, row_tile,
                       row_stride, row_start, idx_out, &k_eff);
@@ -152,6 +164,8 @@ int wf_causal_topk(const void* q_addr, const void* k_addr, int32_t dtype, int64_
   p.rt = row_tile; p.rs = row_stride; p.r0 = row_start;
   p.idx = idx_out;
   p.status = status;
+  p.ws = workspace;
+  p.ws_bytes = workspace_bytes;
   rc = wf::launch_causal_topk(p, dtype, static_cast<cudaStream_t>(stream));
   if (rc) return cuda_fail(rc, "wf_causal_topk");
   return ok();
@@ -193,8 +207,8 @@ int wf_fused_sparse_attention(const void* q_addr, const void* k_addr, int32_t ad
                               int64_t Tk, int32_t D, const int64_t* q_strides, const int64_t* k_strides,
                               const int64_t* v_strides, int32_t top_k, float scale, int32_t pad_mode,
                               int32_t row_tile, int32_t row_stride, int32_t row_start, int32_t* idx_out,
-                              void* out, int32_t out_dtype, const int64_t* out_strides, int32_t* status,
-                              void* stream) {
+                              void* out, int32_t out_dtype, const int64_t* out_strides, void* workspace,
+                              size_t workspace_bytes, int32_t* status, void* stream) {
   int32_t k_eff = 0;
   int32_t rt = row_tile, rs = row_stride, r0 = row_start;
   int rc = check_topk(q_addr, k_addr, addr_dtype, B, Tq, Tk, R, q_addr_strides, k_addr_strides, top_k, pad_mode,
@@ -206,7 +220,7 @@ int wf_fused_sparse_attention(const void* q_addr, const void* k_addr, int32_t ad
                   scale, pad_mode == WF_PAD_MASKED ? WF_ATTN_MASK_NEGATIVE : 0, out, out_dtype, out_strides);
   if (rc) return rc;
   rc = wf_causal_topk(q_addr, k_addr, addr_dtype, B, Tq, Tk, R, q_addr_strides, k_addr_strides, top_k, pad_mode,
-                      row_tile, row_stride, row_start, idx_out, status, stream);
+                      row_tile, row_stride, row_start, idx_out, workspace, workspace_bytes, status, stream);
   if (rc) return rc;
   return wf_sparse_attention(q, k, v, dtype, idx_out, B, H, Tq, Tk, D, k_eff, q_strides, k_strides, v_strides,
                              idx_strides, scale, pad_mode == WF_PAD_MASKED ? WF_ATTN_MASK_NEGATIVE : 0, out,

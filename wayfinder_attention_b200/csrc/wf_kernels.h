@@ -23,6 +23,8 @@ struct TopkParams {
   int32_t* idx;
   int cap;               // candidate buffer capacity per row (multiple of 32)
   int32_t* status;       // nullable; bit 1 set if a bounded wait timed out
+  void* ws;              // workspace of the tensor-core kernel (see topk_tc_workspace_bytes)
+  size_t ws_bytes;
 };
 
 // Sparse attention over retrieved rows, indices shared across heads.
@@ -53,6 +55,8 @@ int launch_sparse_attention(const AttnParams& p, int dtype, int out_dtype, cudaS
 // Tk <= 65536, unit address stride, 16-byte aligned rows.
 bool topk_tc_supported(const TopkParams& p, int dtype);
 int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream);
+// Workspace bytes the tensor-core path needs for B*Tq query rows (0 if K > 128).
+size_t topk_tc_workspace_bytes(int64_t B, int64_t Tq, int K);
 
 // Shared-memory bytes the top-K kernel needs for (R, K); 0 if unsupported.
 size_t topk_smem_bytes(int R, int K);

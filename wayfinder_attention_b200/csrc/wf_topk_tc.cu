@@ -28,9 +28,10 @@
 //           key rows: the arithmetic of the CUDA-core kernel), then appended to
 //           the row's candidate buffer.  A full buffer is compacted to its exact
 //           top-K (warp radix select), which raises the admission threshold.
-//   merge   each CTA reduces its rows to their exact top-K; CTA r then merges
-//           its own and its peer's candidates (read through DSMEM) for rows
-//           [64r, 64r+64), sorts them and writes the output.
+//   output  each CTA writes its rows' exact candidates (about 1.3 K per row) to a
+//           caller-provided workspace; topk_finalize_kernel, launched right
+//           after at full occupancy (one warp per row), selects the exact top-K
+//           of the two lists, sorts it and writes the indices and pads.
 // The margin, 2^-13 * sum_d |q_d| * max|k|, exceeds any plausible accumulation
 // error of a 32-term fp32 dot product with exact bf16/fp16 products, so every
 // key whose exact score reaches the K-th best is admitted: the result is exact
@@ -62,6 +63,9 @@ constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr float kEpsScale = 1.0f / 8192.0f;
 constexpr int kMaxDevices = 64;
 constexpr size_t kMaxSmem = 232448;
+#ifndef WF_TOPK_SKIP
+#define WF_TOPK_SKIP 0  // profiling builds only: bit mask of phases to skip
+#endif
 
 struct TcParams {
   const void* q;
@@ -71,6 +75,8 @@ struct TcParams {
   int rt, rs, r0;
   int32_t* idx;
   int32_t* status;
+  uint64_t* ws;      // [B*Tq][2][CAP] candidate composites (key << 32 | ~index)
+  int32_t* ws_cnt;   // [B*Tq][2] candidate counts
 };
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -87,11 +93,10 @@ struct Layout {
   static constexpr size_t off_k = align_up(Q_BYTES, 1024);
   static constexpr size_t off_kmax = off_k + S * STAGE_STRIDE;
   static constexpr size_t off_bar = align_up(off_kmax + sizeof(float) * S, 8);
-  static constexpr size_t n_bar = 3 * S + 4;  // full, mdone, done, qbar, xbar, rbar, dbar
+  static constexpr size_t n_bar = 3 * S + 2;  // full, mdone, done, qbar, xbar
   static constexpr size_t off_misc = off_bar + 8 * n_bar;  // tmem base, kmax own, kmax peer, abort
   static constexpr size_t off_theta = align_up(off_misc + 16, 16);
-  static constexpr size_t off_cnt = off_theta + 4 * kM;
-  static constexpr size_t off_queue = off_cnt + 4 * kM;
+  static constexpr size_t off_queue = off_theta + 4 * kM;
   static constexpr size_t off_bkey = off_queue + 4 * (size_t)kQcap * kEpiWarps;
   static constexpr size_t KEY_STRIDE = CAP + 1;  // words: odd stride keeps row-private appends conflict-free
   static constexpr size_t IDX_STRIDE = CAP + 2;  // halfwords
@@ -152,13 +157,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* done = mdone + S;
   uint64_t* qbar = done + S;
   uint64_t* xbar = qbar + 1;  // peer posted its pass-1 bound
-  uint64_t* rbar = qbar + 2;  // peer's candidate buffers are final
-  uint64_t* dbar = qbar + 3;  // peer finished reading our buffers
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(base + L::off_misc);
   uint32_t* kmax_own_s = tmem_base_s + 1;
   uint32_t* kmax_in_s = tmem_base_s + 2;
   float* theta_in = reinterpret_cast<float*>(base + L::off_theta);
-  int* cnt_s = reinterpret_cast<int*>(base + L::off_cnt);
   uint32_t* queues = reinterpret_cast<uint32_t*>(base + L::off_queue);
   uint32_t* bkey = reinterpret_cast<uint32_t*>(base + L::off_bkey);
   uint16_t* bidx = reinterpret_cast<uint16_t*>(base + L::off_bidx);
@@ -185,8 +187,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(qbar, 1);
     mbar_init(xbar, kM);
-    mbar_init(rbar, kM);
-    mbar_init(dbar, kM);
     *kmax_own_s = 0u;
     fence_mbarrier_init();
   }
@@ -391,6 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     auto flush = [&](const unsigned char* stage, int c) {
       __syncwarp();
+      if (WF_TOPK_SKIP & 1) { qsize = 0; return; }
       for (int e = lane; e < qsize; e += 32) {
         const uint32_t ent = queue[e];
         const int lr = ent & 31, jj = (ent >> 5) & 127, dest = (int)(ent >> 12);
@@ -467,93 +468,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     (void)mykey;
 
-    // ---------------- own exact top-K per row, then publish to the peer
-    {
-      unsigned need = __ballot_sync(kFullMask, cnt > p.K);
-      while (need) {
-        const int ln = __ffs(need) - 1;
-        need &= need - 1;
-        const int rr = 32 * warp + ln;
-        const int n = __shfl_sync(kFullMask, cnt, ln);
-        merge_row<EPL>(bkey + rr * L::KEY_STRIDE, bidx + rr * L::IDX_STRIDE, n, p.K, lane);
-        if (lane == ln) cnt = p.K;
-      }
-    }
-    cnt_s[r] = cnt;
-    __syncwarp();
-    __threadfence();
-    // The final merge below reads rows other warps of this CTA built: sync the
-    // four selection warps (named barrier 1; the producer warp is not part of it).
-    asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
-    mbar_arrive_peer(map_peer(rbar, peer));
-    if (!warp_wait_cluster(rbar, 0)) { ok = false; why |= 1024; }
-
-    // ---------------- merge own + peer candidates for rows [64 rank, 64 rank + 64)
-    for (int i = 0; i < 16; ++i) {
-      const int rr = 64 * (int)rank + 16 * warp + i;
+    // ---------------- publish this CTA's exact candidates to the workspace
+    // (selection of the final top-K and the sort run in topk_finalize_kernel,
+    // at full occupancy, instead of on these four latency-bound warps)
+    for (int ln = 0; ln < 32; ++ln) {
+      const int rr = 32 * warp + ln;
       if (rr >= nrows) break;
-      uint32_t* bk = bkey + rr * L::KEY_STRIDE;
-      uint16_t* bi = bidx + rr * L::IDX_STRIDE;
-      const int n1 = cnt_s[rr];
-      const int n2 = (int)ld_peer_u32(map_peer(&cnt_s[rr], peer));
-      const uint32_t pk = map_peer(bk, peer);
-      const uint32_t pi = map_peer(bi, peer);
-      uint32_t kk[EPLF];
-      int ii[EPLF];
-#pragma unroll
-      for (int t = 0; t < EPLF; ++t) {
-        const int e = t * 32 + lane;
-        if (e < n1) {
-          kk[t] = bk[e];
-          ii[t] = bi[e];
-        } else if (e < n1 + n2) {
-          kk[t] = ld_peer_u32(pk + 4 * (e - n1));
-          ii[t] = (int)ld_peer_u16(pi + 2 * (e - n1));
-        } else {
-          kk[t] = 0u;
-          ii[t] = INT_MAX;
-        }
-      }
-      __syncwarp();
-      int n = n1 + n2;
-      if (n > p.K) {
-        select_compact<EPLF>(kk, ii, n, p.K, lane, bk, bi);
-        n = p.K;
-      } else {
-#pragma unroll
-        for (int t = 0; t < EPLF; ++t) {
-          const int e = t * 32 + lane;
-          if (e < n) {
-            bk[e] = kk[t];
-            bi[e] = (uint16_t)ii[t];
-          }
-        }
-        __syncwarp();
-      }
-      uint64_t cc[SE];
-#pragma unroll
-      for (int t = 0; t < SE; ++t) {
-        const int e = t * 32 + lane;
-        cc[t] = (e < n) ? (((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e])) : 0ull;
-      }
-      bitonic_sort_desc<SE>(cc, lane);
-      const int gg = g0 + rr;
-      int32_t* out = p.idx + ((int64_t)b * p.Tq + l0 + rr) * p.K;
-#pragma unroll
-      for (int t = 0; t < SE; ++t) {
-        const int s = t * 32 + lane;
-        if (s < p.K) {
-          int val;
-          if (s < n) val = (int)(~(uint32_t)cc[t]);
-          else val = p.pad_mode == 0 ? (int)(((int64_t)gg + p.K + s + 1) % p.Tk) : -1;
-          out[s] = val;
-        }
-      }
-      __syncwarp();
+      const int n = __shfl_sync(kFullMask, cnt, ln);
+      const int64_t row = (int64_t)b * p.Tq + l0 + rr;
+      uint64_t* dst = p.ws + (row * 2 + rank) * CAP;
+      const uint32_t* bk = bkey + rr * L::KEY_STRIDE;
+      const uint16_t* bi = bidx + rr * L::IDX_STRIDE;
+      for (int e = lane; e < n; e += 32) dst[e] = ((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e]);
+      if (lane == 0) p.ws_cnt[row * 2 + rank] = n;
     }
-    __syncwarp();
-    mbar_arrive_peer(map_peer(dbar, peer));
-    if (!warp_wait_cluster(dbar, 0)) { ok = false; why |= 2048; }
   }
   if (!ok && p.status) atomicOr(p.status, 2 | (int)why);
 
@@ -562,6 +490,83 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- finalisation
+// One warp per query row: the exact top-K of the two CTAs' candidate lists
+// (composites key << 32 | ~index, so larger = better and ties favour the lower
+// index), sorted descending, plus pad slots.  Runs at full occupancy; the
+// selection is the same warp radix select the streaming kernels use.
+struct FinParams {
+  const uint64_t* ws;
+  const int32_t* ws_cnt;
+  int32_t* idx;
+  int B, Tq, Tk, K, cap;
+  int pad_mode;
+  int rt, rs, r0;
+};
+
+constexpr int kFinWarps = 8;
+
+template <int EPLF, int SE>
+__global__ void __launch_bounds__(kFinWarps * 32) topk_finalize_kernel(const FinParams p) {
+  __shared__ uint32_t skey[kFinWarps][32 * SE];
+  __shared__ int sidx[kFinWarps][32 * SE];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kFinWarps + warp;
+  if (row >= (int64_t)p.B * p.Tq) return;
+  const int l = (int)(row % p.Tq);
+  const int g = ((l / p.rt) * p.rs + p.r0) * p.rt + (l % p.rt);
+  const int n1 = p.ws_cnt[row * 2], n2 = p.ws_cnt[row * 2 + 1];
+  const int n = n1 + n2;
+  const uint64_t* a = p.ws + row * 2 * p.cap;
+  const uint64_t* bsrc = a + p.cap;
+  uint32_t kk[EPLF];
+  int ii[EPLF];
+#pragma unroll
+  for (int t = 0; t < EPLF; ++t) {
+    const int e = t * 32 + lane;
+    uint64_t c = 0;
+    if (e < n1) c = a[e];
+    else if (e < n) c = bsrc[e - n1];
+    kk[t] = (uint32_t)(c >> 32);
+    ii[t] = e < n ? (int)(~(uint32_t)c) : INT_MAX;
+  }
+  uint32_t* bk = skey[warp];
+  int* bi = sidx[warp];
+  int m = n;
+  if (n > p.K) {
+    select_compact<EPLF>(kk, ii, n, p.K, lane, bk, bi);
+    m = p.K;
+  } else {
+#pragma unroll
+    for (int t = 0; t < EPLF; ++t) {
+      const int e = t * 32 + lane;
+      if (e < n) {
+        bk[e] = kk[t];
+        bi[e] = ii[t];
+      }
+    }
+    __syncwarp();
+  }
+  uint64_t cc[SE];
+#pragma unroll
+  for (int t = 0; t < SE; ++t) {
+    const int e = t * 32 + lane;
+    cc[t] = (e < m) ? (((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e])) : 0ull;
+  }
+  bitonic_sort_desc<SE>(cc, lane);
+  int32_t* out = p.idx + row * p.K;
+#pragma unroll
+  for (int t = 0; t < SE; ++t) {
+    const int s = t * 32 + lane;
+    if (s < p.K) {
+      int val;
+      if (s < m) val = (int)(~(uint32_t)cc[t]);
+      else val = p.pad_mode == 0 ? (int)(((int64_t)g + p.K + s + 1) % p.Tk) : -1;
+      out[s] = val;
+    }
   }
 }
 
@@ -646,6 +651,11 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
   t.rt = p.rt; t.rs = p.rs; t.r0 = p.r0;
   t.idx = p.idx;
   t.status = p.status;
+  const size_t rows = (size_t)p.B * p.Tq;
+  const size_t need = rows * 2 * L::CAP * sizeof(uint64_t) + rows * 2 * sizeof(int32_t);
+  if (!p.ws || p.ws_bytes < need || reinterpret_cast<uintptr_t>(p.ws) % 16) return -3;
+  t.ws = reinterpret_cast<uint64_t*>(p.ws);
+  t.ws_cnt = reinterpret_cast<int32_t*>(t.ws + rows * 2 * L::CAP);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * ((p.Tq + kM - 1) / kM), p.B);
@@ -661,6 +671,14 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, kern, qmap, kmap, t);
   if (e != cudaSuccess) return (int)e;
+  FinParams f{};
+  f.ws = t.ws;
+  f.ws_cnt = t.ws_cnt;
+  f.idx = p.idx;
+  f.B = p.B; f.Tq = p.Tq; f.Tk = p.Tk; f.K = p.K; f.cap = L::CAP;
+  f.pad_mode = p.pad_mode;
+  f.rt = p.rt; f.rs = p.rs; f.r0 = p.r0;
+  topk_finalize_kernel<2 * EPL, SE><<<(unsigned)((rows + kFinWarps - 1) / kFinWarps), kFinWarps * 32, 0, stream>>>(f);
   return (int)cudaGetLastError();
 }
 
@@ -696,6 +714,13 @@ bool topk_tc_supported(const TopkParams& p, int dtype) {
   const bool identity = p.rs == 1 && p.r0 == 0;
   if (!identity && p.rt % kM) return false;
   return encode_fn() != nullptr;
+}
+
+size_t topk_tc_workspace_bytes(int64_t B, int64_t Tq, int K) {
+  const int cap = K <= 32 ? 128 : K <= 64 ? 160 : K <= 128 ? 224 : 0;
+  if (!cap) return 0;
+  const size_t rows = (size_t)B * Tq;
+  return rows * 2 * cap * sizeof(uint64_t) + rows * 2 * sizeof(int32_t);
 }
 
 int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream) {

@@ -177,13 +177,15 @@ def fused_sparse_attention(
     out = torch.empty(B, H, T, D, dtype=out_dtype or q.dtype, device=dev)
     if status is not None and (status.dtype != torch.int32 or not status.is_cuda):
         raise ValueError("status must be an int32 CUDA tensor")
+    ws = _lib.workspace(B, T, T, R, int(top_k), qa.dtype, dev)
     with torch.cuda.device(dev):
         rc = lib.wf_fused_sparse_attention(
             qa.data_ptr(), ka.data_ptr(), _lib.dtype_code(qa.dtype), R, _lib.strides(qa), _lib.strides(ka),
             q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.dtype_code(q.dtype), B, H, T, T, D,
             _lib.strides(q), _lib.strides(k), _lib.strides(v), int(top_k), float(scale),
             pad_mode_code(pad_mode), 0, 1, 0, idx.data_ptr(), out.data_ptr(), _lib.dtype_code(out.dtype),
-            _lib.strides(out), status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
+            _lib.strides(out), ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+            status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
         )
     _lib.check(rc)
     return out, idx
