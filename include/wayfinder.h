@@ -96,6 +96,24 @@ WF_API size_t wf_causal_topk_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, 
                                              int32_t dtype);
 
 /*
+ * Allocation-free variant of wf_causal_topk.  It has no counterpart in the
+ * reference.  It is for callers that cannot allocate device memory at all (an
+ * allocator-less runtime, or code running where cudaMalloc is not permitted): the
+ * retrieval scratch comes from a fixed 8 MiB device array built into this library,
+ * which every GPU that loads the library keeps reserved until the process exits.
+ * Same arguments and results as wf_causal_topk without the workspace; B*Tq is
+ * limited to what fits in that array (2335 query rows at K = 128; larger requests
+ * return WF_ERR_UNSUPPORTED with the byte counts).  The first call on a device
+ * looks up the array's device address, so make that first call before any stream
+ * capture.  All calls share the one array: calls that overlap on the GPU (other
+ * streams, other host threads) race on it and must be serialised by the caller.
+ */
+WF_API int wf_causal_topk_noalloc(const void* q_addr, const void* k_addr, int32_t dtype, int64_t B, int64_t Tq,
+                                  int64_t Tk, int32_t R, const int64_t* q_strides, const int64_t* k_strides,
+                                  int32_t top_k, int32_t pad_mode, int32_t row_tile, int32_t row_stride,
+                                  int32_t row_start, int32_t* idx_out, int32_t* status, void* stream);
+
+/*
  * Softmax attention over the K rows named by idx, shared by all heads.  Replaces
  * sparse_meat_attention() (routing_attention/kernels/fused_sparse.py:275-324; the
  * arithmetic of sparse_meat_attention_reference :80-94), computed in fp32.

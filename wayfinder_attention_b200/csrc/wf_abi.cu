@@ -227,4 +227,26 @@ int wf_fused_sparse_attention(const void* q_addr, const void* k_addr, int32_t ad
                              out_dtype, out_strides, status, stream);
 }
 
+int wf_causal_topk_noalloc(const void* q_addr, const void* k_addr, int32_t dtype, int64_t B, int64_t Tq,
+                           int64_t Tk, int32_t R, const int64_t* q_strides, const int64_t* k_strides,
+                           int32_t top_k, int32_t pad_mode, int32_t row_tile, int32_t row_stride,
+                           int32_t row_start, int32_t* idx_out, int32_t* status, void* stream) {
+  // Same retrieval as wf_causal_topk, with the scratch taken from the library's
+  // built-in device array instead of a caller workspace; no allocation anywhere.
+  const size_t need = wf_causal_topk_workspace_bytes(B, Tq, Tk, R, top_k, dtype);
+  void* scratch = nullptr;
+  if (need > 0) {
+    const size_t cap = wf::noalloc_scratch_capacity();
+    if (need > cap)
+      return fail(WF_ERR_UNSUPPORTED,
+                  "wf_causal_topk_noalloc: B*Tq=%lld query rows need %zu bytes of scratch but the built-in "
+                  "buffer holds %zu; use wf_causal_topk with a workspace",
+                  (long long)(B * Tq), need, cap);
+    const int rc = wf::noalloc_scratch(&scratch);
+    if (rc) return cuda_fail(rc, "wf_causal_topk_noalloc: scratch address lookup");
+  }
+  return wf_causal_topk(q_addr, k_addr, dtype, B, Tq, Tk, R, q_strides, k_strides, top_k, pad_mode, row_tile,
+                        row_stride, row_start, idx_out, scratch, need, status, stream);
+}
+
 }  // extern "C"

@@ -55,6 +55,11 @@ int launch_sparse_attention(const AttnParams& p, int dtype, int out_dtype, cudaS
 // Tk <= 65536, unit address stride, 16-byte aligned rows.
 bool topk_tc_supported(const TopkParams& p, int dtype);
 int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream);
+// Allocation-free retrieval: capacity of the library's built-in scratch array and
+// its device address on the current device (first call per device looks it up).
+size_t noalloc_scratch_capacity();
+int noalloc_scratch(void** out);
+
 // Workspace bytes the tensor-core path needs for B*Tq query rows (0 if K > 128).
 size_t topk_tc_workspace_bytes(int64_t B, int64_t Tq, int K);
 

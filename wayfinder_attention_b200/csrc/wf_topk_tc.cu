@@ -42,6 +42,7 @@
 #include "wf_select.cuh"
 #include "wf_sm100.cuh"
 
+#include <mutex>
 #include <type_traits>
 
 namespace wf {
@@ -729,5 +730,39 @@ int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream) {
   return -1;
 }
 
-}  // namespace wf
+// ---------------------------------------------------------------- allocation-free scratch
+// Retrieval scratch for callers that cannot allocate device memory at all.  This
+// array is part of the library image: every GPU that loads the library reserves
+// kNoAllocScratchBytes for it until the process exits.  All calls share it and it
+// keeps the previous call's contents; nothing in it needs to start at zero,
+// because the retrieval kernel writes every count and candidate it later reads.
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB: B*Tq <= 2335 query rows at K = 128
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+}  // namespace
+
+size_t noalloc_scratch_capacity() { return kNoAllocScratchBytes; }
+
+// Device address of the scratch array on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address comes from
+// cudaGetSymbolAddress, queried once per device with that device current.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return (int)e;
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace wf
