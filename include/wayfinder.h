@@ -89,8 +89,8 @@ WF_API int wf_causal_topk(const void* q_addr, const void* k_addr, int32_t dtype,
 /*
  * Device workspace (bytes, 16-byte aligned) that wf_causal_topk and
  * wf_fused_sparse_attention need for these sizes: the tensor-core retrieval
- * kernel parks each row's exact candidates there (about 7 KB per query row at
- * K = 128) for its finalisation pass.  0 means none is needed.
+ * kernel parks each row's exact candidates there (about 4 KB per query row for
+ * K <= 128) for its finalisation pass.  0 means none is needed.
  */
 WF_API size_t wf_causal_topk_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, int32_t R, int32_t top_k,
                                              int32_t dtype);
@@ -102,7 +102,7 @@ WF_API size_t wf_causal_topk_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, 
  * retrieval scratch comes from a fixed 8 MiB device array built into this library,
  * which every GPU that loads the library keeps reserved until the process exits.
  * Same arguments and results as wf_causal_topk without the workspace; B*Tq is
- * limited to what fits in that array (2335 query rows at K = 128; larger requests
+ * limited to what fits in that array (2044 query rows for K <= 128; larger requests
  * return WF_ERR_UNSUPPORTED with the byte counts).  The first call on a device
  * looks up the array's device address, so make that first call before any stream
  * capture.  All calls share the one array: calls that overlap on the GPU (other

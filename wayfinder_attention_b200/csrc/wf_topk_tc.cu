@@ -28,8 +28,8 @@
 //           key rows: the arithmetic of the CUDA-core kernel), then appended to
 //           the row's candidate buffer.  A full buffer is compacted to its exact
 //           top-K (warp radix select), which raises the admission threshold.
-//   output  each CTA writes its rows' exact candidates (about 1.3 K per row) to a
-//           caller-provided workspace; topk_finalize_kernel, launched right
+//   output  rescored candidates go straight to a caller-provided workspace
+//           (256 slots per row and CTA; a full slice is compacted to its exact top-K); topk_finalize_kernel, launched right
 //           after at full occupancy (one warp per row), selects the exact top-K
 //           of the two lists, sorts it and writes the indices and pads.
 // The margin, 2^-13 * sum_d |q_d| * max|k|, exceeds any plausible accumulation
@@ -59,6 +59,7 @@ constexpr int kEpiWarps = 4;
 constexpr int kThreads = (kEpiWarps + 1) * 32;
 constexpr int kGroups = 256;  // pass-1 key groups per row (TMEM columns 256..511)
 constexpr int kQcap = 1024;   // rescoring queue entries per warp
+constexpr int kWcap = 256;    // workspace candidates per (row, CTA); a full row is compacted to its top-K
 constexpr unsigned kFullMask = 0xffffffffu;
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr float kEpsScale = 1.0f / 8192.0f;
@@ -76,7 +77,7 @@ struct TcParams {
   int rt, rs, r0;
   int32_t* idx;
   int32_t* status;
-  uint64_t* ws;      // [B*Tq][2][CAP] candidate composites (key << 32 | ~index)
+  uint64_t* ws;      // [B*Tq][2][kWcap] candidate composites (key << 32 | ~index)
   int32_t* ws_cnt;   // [B*Tq][2] candidate counts
 };
 
@@ -86,7 +87,6 @@ template <int R, int EPL>
 struct Layout {
   static constexpr int ROWB = R * 2;
   static constexpr int S = R >= 64 ? 2 : 3;  // shared-memory stages
-  static constexpr int CAP = 32 * EPL;
   static constexpr size_t Q_BYTES = (size_t)kM * ROWB;
   static constexpr size_t STAGE_BYTES = (size_t)kN * ROWB;
   static constexpr size_t STAGE_STRIDE = align_up(STAGE_BYTES, 1024);
@@ -98,12 +98,12 @@ struct Layout {
   static constexpr size_t off_misc = off_bar + 8 * n_bar;  // tmem base, kmax own, kmax peer, abort
   static constexpr size_t off_theta = align_up(off_misc + 16, 16);
   static constexpr size_t off_queue = off_theta + 4 * kM;
-  static constexpr size_t off_bkey = off_queue + 4 * (size_t)kQcap * kEpiWarps;
-  static constexpr size_t KEY_STRIDE = CAP + 1;  // words: odd stride keeps row-private appends conflict-free
-  static constexpr size_t IDX_STRIDE = CAP + 2;  // halfwords
-  static constexpr size_t off_bidx = off_bkey + sizeof(uint32_t) * kM * KEY_STRIDE;
-  static constexpr size_t bytes = off_bidx + sizeof(uint16_t) * kM * IDX_STRIDE;
-  static constexpr size_t smem = bytes + 1024;  // slack to align the dynamic base to 1024
+  static constexpr size_t off_merge = off_queue + 4 * (size_t)kQcap * kEpiWarps;  // per warp: K keys + K indices
+  static constexpr size_t bytes = off_merge + (size_t)kEpiWarps * 128 * (4 + 4);
+  // Slack to align the dynamic base to 1024, and at least 116 KB in total: two of
+  // these CTAs must never share an SM (each allocates all 512 TMEM columns), while
+  // sparse-attention blocks (37 KB) may run beside one.
+  static constexpr size_t smem = bytes + 1024 > 116 * 1024 ? bytes + 1024 : 116 * 1024;
 };
 
 // Exact fp32 score of q-tile row qr and stage row kr, both stored with the TMA
@@ -142,7 +142,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = Layout<R, EPL>;
   constexpr int S = L::S;
   constexpr int ROWB = L::ROWB;
-  constexpr int CAP = L::CAP;
   constexpr int KSTEPS = R / 16;
   constexpr uint32_t TMEM_COLS = 512;
   constexpr bool kBf16 = !std::is_same<TI, __half>::value;
@@ -163,8 +162,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* kmax_in_s = tmem_base_s + 2;
   float* theta_in = reinterpret_cast<float*>(base + L::off_theta);
   uint32_t* queues = reinterpret_cast<uint32_t*>(base + L::off_queue);
-  uint32_t* bkey = reinterpret_cast<uint32_t*>(base + L::off_bkey);
-  uint16_t* bidx = reinterpret_cast<uint16_t*>(base + L::off_bidx);
+  uint32_t* mkey = reinterpret_cast<uint32_t*>(base + L::off_merge);       // [warp][128]
+  int* midx = reinterpret_cast<int*>(mkey + kEpiWarps * 128);              // [warp][128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -383,23 +382,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float eps = kEpsScale * qabs * kpair;
     float lim = theta > -INFINITY ? theta - eps : -INFINITY;
 
-    // ---------------- pass 2: admit, rescore exactly, keep candidates
+    // ---------------- pass 2: admit, rescore exactly, keep candidates in the workspace
     uint32_t* queue = queues + warp * kQcap;
-    uint32_t* mykey = bkey + r * L::KEY_STRIDE;
+    const int64_t row0 = (int64_t)b * p.Tq + l0 + 32 * warp;  // first row of this warp
     int cnt = 0;
     int qsize = 0;  // warp-uniform
-    const uint32_t ltmask = lanemask_lt();
 
     auto flush = [&](const unsigned char* stage, int c) {
       __syncwarp();
-      if (WF_TOPK_SKIP & 1) { qsize = 0; return; }
       for (int e = lane; e < qsize; e += 32) {
         const uint32_t ent = queue[e];
         const int lr = ent & 31, jj = (ent >> 5) & 127, dest = (int)(ent >> 12);
-        const int row = 32 * warp + lr;
-        const float ex = dot_swizzled<TI, ROWB>(qs, row, stage, jj);
-        bkey[row * L::KEY_STRIDE + dest] = ordered_key(ex);
-        bidx[row * L::IDX_STRIDE + dest] = (uint16_t)(c * kN + jj);
+        const float ex = dot_swizzled<TI, ROWB>(qs, 32 * warp + lr, stage, jj);
+        p.ws[((row0 + lr) * 2 + rank) * kWcap + dest] =
+            ((uint64_t)ordered_key(ex) << 32) | (uint32_t)(~(uint32_t)(c * kN + jj));
       }
       __syncwarp();
       qsize = 0;
@@ -424,24 +420,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int room = g - (c * kN + sl * 32);
         if (!row_ok || room < 0) m = 0;
         else if (room < 31) m &= (2u << room) - 1u;
-        int np = __popc(m);
-        // rows whose buffer would overflow: rescore what is pending, then compact them
-        unsigned need = __ballot_sync(kFullMask, cnt + np > CAP);
+        const int np = __popc(m);
+        // rows whose workspace slice would overflow: rescore what is pending, then
+        // compact them to their exact top-K (rare: about 1.3 K keys per row are admitted)
+        unsigned need = __ballot_sync(kFullMask, cnt + np > kWcap);
         if (need) {
           flush(stage, c);
           while (need) {
             const int ln = __ffs(need) - 1;
             need &= need - 1;
-            const int rr = 32 * warp + ln;
             const int n = __shfl_sync(kFullMask, cnt, ln);
-            const uint32_t tau = merge_row<EPL>(bkey + rr * L::KEY_STRIDE, bidx + rr * L::IDX_STRIDE, n, p.K, lane);
+            uint64_t* wrow = p.ws + ((row0 + ln) * 2 + rank) * kWcap;
+            uint32_t kk[kWcap / 32];
+            int ii[kWcap / 32];
+#pragma unroll
+            for (int t = 0; t < kWcap / 32; ++t) {
+              const int e = t * 32 + lane;
+              const uint64_t cv = e < n ? wrow[e] : 0ull;
+              kk[t] = (uint32_t)(cv >> 32);
+              ii[t] = e < n ? (int)(~(uint32_t)cv) : INT_MAX;
+            }
+            uint32_t* bk = mkey + warp * 128;
+            int* bi = midx + warp * 128;
+            const uint32_t tau = select_compact<kWcap / 32>(kk, ii, n, p.K, lane, bk, bi);
+            for (int e = lane; e < p.K; e += 32) wrow[e] = ((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e]);
+            __syncwarp();
             if (lane == ln) {
               cnt = p.K;
               lim = fmaxf(lim, key_to_float(tau) - eps);
             }
           }
         }
-        // queue the admitted (row, key) pairs with their buffer slots
+        // queue the admitted (row, key) pairs with their workspace slots
         int incl = np;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -460,29 +470,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         cnt += np;
         qsize += total;
-        (void)ltmask;
       }
       flush(stage, c);  // the stage is about to be released
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&done[s]);
     }
-    (void)mykey;
-
-    // ---------------- publish this CTA's exact candidates to the workspace
-    // (selection of the final top-K and the sort run in topk_finalize_kernel,
-    // at full occupancy, instead of on these four latency-bound warps)
-    for (int ln = 0; ln < 32; ++ln) {
-      const int rr = 32 * warp + ln;
-      if (rr >= nrows) break;
-      const int n = __shfl_sync(kFullMask, cnt, ln);
-      const int64_t row = (int64_t)b * p.Tq + l0 + rr;
-      uint64_t* dst = p.ws + (row * 2 + rank) * CAP;
-      const uint32_t* bk = bkey + rr * L::KEY_STRIDE;
-      const uint16_t* bi = bidx + rr * L::IDX_STRIDE;
-      for (int e = lane; e < n; e += 32) dst[e] = ((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e]);
-      if (lane == 0) p.ws_cnt[row * 2 + rank] = n;
-    }
+    if (row_ok) p.ws_cnt[(row0 + lane) * 2 + rank] = cnt;
   }
   if (!ok && p.status) atomicOr(p.status, 2 | (int)why);
 
@@ -511,15 +505,10 @@ struct FinParams {
 constexpr int kFinWarps = 8;
 
 template <int EPLF, int SE>
-__global__ void __launch_bounds__(kFinWarps * 32) topk_finalize_kernel(const FinParams p) {
-  __shared__ uint32_t skey[kFinWarps][32 * SE];
-  __shared__ int sidx[kFinWarps][32 * SE];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * kFinWarps + warp;
-  if (row >= (int64_t)p.B * p.Tq) return;
+__device__ __forceinline__ void finalize_row(const FinParams& p, int64_t row, int n1, int n2, int lane,
+                                             uint32_t* bk, int* bi) {
   const int l = (int)(row % p.Tq);
   const int g = ((l / p.rt) * p.rs + p.r0) * p.rt + (l % p.rt);
-  const int n1 = p.ws_cnt[row * 2], n2 = p.ws_cnt[row * 2 + 1];
   const int n = n1 + n2;
   const uint64_t* a = p.ws + row * 2 * p.cap;
   const uint64_t* bsrc = a + p.cap;
@@ -534,8 +523,6 @@ __global__ void __launch_bounds__(kFinWarps * 32) topk_finalize_kernel(const Fin
     kk[t] = (uint32_t)(c >> 32);
     ii[t] = e < n ? (int)(~(uint32_t)c) : INT_MAX;
   }
-  uint32_t* bk = skey[warp];
-  int* bi = sidx[warp];
   int m = n;
   if (n > p.K) {
     select_compact<EPLF>(kk, ii, n, p.K, lane, bk, bi);
@@ -569,6 +556,19 @@ __global__ void __launch_bounds__(kFinWarps * 32) topk_finalize_kernel(const Fin
       out[s] = val;
     }
   }
+}
+
+template <int SE>
+__global__ void __launch_bounds__(kFinWarps * 32, 2) topk_finalize_kernel(const FinParams p) {
+  __shared__ uint32_t skey[kFinWarps][128];
+  __shared__ int sidx[kFinWarps][128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kFinWarps + warp;
+  if (row >= (int64_t)p.B * p.Tq) return;
+  const int n1 = p.ws_cnt[row * 2], n2 = p.ws_cnt[row * 2 + 1];
+  // typical rows hold about 2.6 K candidates; the wide form covers full workspace slices
+  if (n1 + n2 <= 12 * 32) finalize_row<12, SE>(p, row, n1, n2, lane, skey[warp], sidx[warp]);
+  else finalize_row<2 * kWcap / 32, SE>(p, row, n1, n2, lane, skey[warp], sidx[warp]);
 }
 
 // ---------------------------------------------------------------- host side
@@ -607,13 +607,9 @@ bool make_map(CUtensorMap* map, const void* ptr, bool bf16, int R, int64_t T, in
   return rc == CUDA_SUCCESS;
 }
 
-// (EPL, SE, EPLF) per K class: buffer capacity 32*EPL >= K + 64, sort width 32*SE >= K, merge width 32*EPLF >= 2K.
 template <int R>
 size_t smem_for_k(int K) {
-  if (K <= 32) return Layout<R, 4>::smem;
-  if (K <= 64) return Layout<R, 5>::smem;
-  if (K <= 128) return Layout<R, 7>::smem;
-  return 0;
+  return K <= 128 ? Layout<R, 1>::smem : 0;
 }
 
 size_t tc_smem(int R, int K) {
@@ -653,10 +649,10 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
   t.idx = p.idx;
   t.status = p.status;
   const size_t rows = (size_t)p.B * p.Tq;
-  const size_t need = rows * 2 * L::CAP * sizeof(uint64_t) + rows * 2 * sizeof(int32_t);
+  const size_t need = rows * 2 * kWcap * sizeof(uint64_t) + rows * 2 * sizeof(int32_t);
   if (!p.ws || p.ws_bytes < need || reinterpret_cast<uintptr_t>(p.ws) % 16) return -3;
   t.ws = reinterpret_cast<uint64_t*>(p.ws);
-  t.ws_cnt = reinterpret_cast<int32_t*>(t.ws + rows * 2 * L::CAP);
+  t.ws_cnt = reinterpret_cast<int32_t*>(t.ws + rows * 2 * kWcap);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * ((p.Tq + kM - 1) / kM), p.B);
@@ -676,10 +672,10 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
   f.ws = t.ws;
   f.ws_cnt = t.ws_cnt;
   f.idx = p.idx;
-  f.B = p.B; f.Tq = p.Tq; f.Tk = p.Tk; f.K = p.K; f.cap = L::CAP;
+  f.B = p.B; f.Tq = p.Tq; f.Tk = p.Tk; f.K = p.K; f.cap = kWcap;
   f.pad_mode = p.pad_mode;
   f.rt = p.rt; f.rs = p.rs; f.r0 = p.r0;
-  topk_finalize_kernel<2 * EPL, SE><<<(unsigned)((rows + kFinWarps - 1) / kFinWarps), kFinWarps * 32, 0, stream>>>(f);
+  topk_finalize_kernel<SE><<<(unsigned)((rows + kFinWarps - 1) / kFinWarps), kFinWarps * 32, 0, stream>>>(f);
   return (int)cudaGetLastError();
 }
 
@@ -718,10 +714,9 @@ bool topk_tc_supported(const TopkParams& p, int dtype) {
 }
 
 size_t topk_tc_workspace_bytes(int64_t B, int64_t Tq, int K) {
-  const int cap = K <= 32 ? 128 : K <= 64 ? 160 : K <= 128 ? 224 : 0;
-  if (!cap) return 0;
+  if (K > 128) return 0;
   const size_t rows = (size_t)B * Tq;
-  return rows * 2 * cap * sizeof(uint64_t) + rows * 2 * sizeof(int32_t);
+  return rows * 2 * kWcap * sizeof(uint64_t) + rows * 2 * sizeof(int32_t);
 }
 
 int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream) {
@@ -736,7 +731,7 @@ int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream) {
 // kNoAllocScratchBytes for it until the process exits.  All calls share it and it
 // keeps the previous call's contents; nothing in it needs to start at zero,
 // because the retrieval kernel writes every count and candidate it later reads.
-constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB: B*Tq <= 2335 query rows at K = 128
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB: B*Tq <= 2044 query rows (4104 bytes each) for K <= 128
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
