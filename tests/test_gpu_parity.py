@@ -380,3 +380,22 @@ def test_workspace_too_small_is_rejected(cuda_device):
                             _lib.strides(x["q_addr"]), _lib.strides(x["k_addr"]), 64, 0, 0, 1, 0, idx.data_ptr(),
                             ws.data_ptr(), ws.numel(), None, _lib.stream_ptr(cuda_device))
     assert rc == _lib.WF_ERR_INVALID_ARGUMENT and b"workspace" in lib.wf_last_error()
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_key_vector_module_matches_oracle(fused, cuda_device):
+    """KeyVectorSparseAttention: head-mean search vectors (R = head_dim = 64) through the same kernels."""
+    from wayfinder_attention_b200 import KeyVectorSparseAttention
+
+    torch.manual_seed(45)
+    m = KeyVectorSparseAttention(256, 4, top_k=64, retrieval_config={"use_fused_sparse": fused}).eval()
+    x = torch.randn(2, 300, 256)
+    with torch.no_grad():
+        q = m.q_proj(x).view(2, 300, 4, 64).transpose(1, 2)
+        k = m.k_proj(x).view(2, 300, 4, 64).transpose(1, 2)
+        v = m.v_proj(x).view(2, 300, 4, 64).transpose(1, 2)
+        qs, ks = k.mean(dim=1), q.mean(dim=1)  # the reference's argument order
+        o, _ = oracle.fused_sparse_attention(qs.numpy(), ks.numpy(), q.numpy(), k.numpy(), v.numpy(), 64, 0.125)
+        want = m.out_proj(torch.from_numpy(o).transpose(1, 2).reshape(2, 300, 256))
+    got = m.to(cuda_device)(x.to(cuda_device))
+    assert (got.cpu() - want).abs().max() <= 1e-4

@@ -11,6 +11,7 @@ there is no CPU path.
 
 from ._lib import load_library
 from .attention import (
+    KeyVectorSparseAttention,
     LearnedAddressModule,
     LearnedAddressSparseAttention,
     RetrievalConfig,
@@ -36,6 +37,7 @@ __all__ = [
     "SparseMeatConfig",
     "LearnedAddressModule",
     "LearnedAddressSparseAttention",
+    "KeyVectorSparseAttention",
     "RetrievalConfig",
     "retrieval_config_from_dict",
     "DenseSDPAAttention",

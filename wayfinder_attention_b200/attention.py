@@ -181,3 +181,79 @@ class LearnedAddressSparseAttention(nn.Module):
                 attn_dense.scatter_(2, idx, 1.0 / k_eff)
             return out, attn_dense
         return out
+
+
+class KeyVectorSparseAttention(nn.Module):
+    """Key-vector retrieval baseline (``routing_attention/models/attention.py:296-406``).
+
+    The search vectors are head means of the Q/K projections (R = head_dim) and the
+    same fused retrieval + sparse attention kernels run on them.  The reference's
+    ``_search_vectors(k, q)`` is called as ``_search_vectors(q, k)`` on both of its
+    paths (``attention.py:341-343, 349, 384``), so its *query* search vector is the
+    head mean of the keys and its *key* search vector the head mean of the queries;
+    this module reproduces that.  ``apply_to_key_vector=True`` rounds the search
+    vectors to ``retrieval_config.dtype`` first (the ``RoutingRetriever`` numerics).
+    Rows i < K-1 get the reference pads of ``_finalize_causal_topk`` on every path
+    (the reference's inline path leaves arbitrary masked indices there).
+    """
+
+    def __init__(
+        self,
+        d_model: int,
+        n_heads: int,
+        top_k: int = 32,
+        dropout: float = 0.1,
+        retrieval_config: RetrievalConfig | dict | None = None,
+        pad_mode: str = "reference",
+    ):
+        super().__init__()
+        assert d_model % n_heads == 0
+        self.n_heads = n_heads
+        self.head_dim = d_model // n_heads
+        self.scale = self.head_dim ** -0.5
+        self.top_k = top_k
+        self.pad_mode = pad_mode
+        self._retrieval_cfg = _resolve_retrieval_cfg(retrieval_config, top_k)
+        self.use_fast_retrieval = self._retrieval_cfg.apply_to_key_vector
+        self.q_proj = nn.Linear(d_model, d_model)
+        self.k_proj = nn.Linear(d_model, d_model)
+        self.v_proj = nn.Linear(d_model, d_model)
+        self.out_proj = nn.Linear(d_model, d_model)
+        self.dropout = nn.Dropout(dropout)
+
+    def _search_vectors(self, q: torch.Tensor, k: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """(query search, key search) as the reference computes them: (mean_h k, mean_h q)."""
+        return k.mean(dim=1).contiguous(), q.mean(dim=1).contiguous()
+
+    def forward(self, x: torch.Tensor, attn_mask: Optional[torch.Tensor] = None, return_attention: bool = False,
+                **kwargs):
+        B, T, D = x.shape
+        q = self.q_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
+        k = self.k_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
+        v = self.v_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
+        qs, ks = self._search_vectors(q, k)
+        if self._retrieval_cfg.use_fused_sparse:
+            meat, candidate_idx = fused_sparse_attention(qs, ks, q, k, v, self.top_k, self.scale,
+                                                         pad_mode=self.pad_mode)
+        else:
+            if self.training and self.dropout.p > 0:
+                raise NotImplementedError(
+                    "attention-probability dropout of the non-fused path is not implemented "
+                    "(forward-only kernels); use eval() or retrieval_config.use_fused_sparse=True"
+                )
+            if self.use_fast_retrieval:
+                rdt = _DTYPES.get(self._retrieval_cfg.dtype, torch.float16)
+                qs, ks = qs.to(rdt), ks.to(rdt)
+            candidate_idx = causal_topk(qs, ks, self.top_k, pad_mode=self.pad_mode)
+            meat = sparse_meat_attention(q, k, v, candidate_idx, self.scale,
+                                         mask_negative=self.pad_mode == "masked")
+        out = self.out_proj(meat.transpose(1, 2).contiguous().view(B, T, D))
+        if return_attention:
+            k_eff = candidate_idx.shape[-1]
+            attn_dense = torch.zeros(B, T, T, device=x.device)
+            if k_eff > 0:
+                idx = candidate_idx.long()
+                idx = torch.where(idx >= 0, idx, idx[..., :1])
+                attn_dense.scatter_(2, idx, 1.0 / k_eff)
+            return out, attn_dense
+        return out

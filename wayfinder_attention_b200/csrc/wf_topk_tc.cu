@@ -55,7 +55,7 @@ using select::select_compact;
 
 constexpr int kM = 128;   // query rows per tile = TMEM lanes
 constexpr int kN = 128;   // keys per chunk = MMA N
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant
 constexpr int kThreads = (kEpiWarps + 1) * 32;
 constexpr int kGroups = 256;  // pass-1 key groups per row (TMEM columns 256..511)
 constexpr int kQcap = 1024;   // rescoring queue entries per warp
@@ -97,7 +97,9 @@ struct Layout {
   static constexpr size_t n_bar = 3 * S + 2;  // full, mdone, done, qbar, xbar
   static constexpr size_t off_misc = off_bar + 8 * n_bar;  // tmem base, kmax own, kmax peer, abort
   static constexpr size_t off_theta = align_up(off_misc + 16, 16);
-  static constexpr size_t off_queue = off_theta + 4 * kM;
+  static constexpr size_t off_cnt = off_theta + 4 * kM;   // per-row workspace slot counters
+  static constexpr size_t off_thr = off_cnt + 4 * kM;     // per-row thresholds after a compaction
+  static constexpr size_t off_queue = off_thr + 4 * kM;
   static constexpr size_t off_merge = off_queue + 4 * (size_t)kQcap * kEpiWarps;  // per warp: K keys + K indices
   static constexpr size_t bytes = off_merge + (size_t)kEpiWarps * 128 * (4 + 4);
   // Slack to align the dynamic base to 1024, and at least 116 KB in total: two of
@@ -113,6 +115,20 @@ struct Layout {
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, kWaitLimitNs));
 }
+// Named barrier of the 64 threads of one quadrant's two warps, and its OR-reduction.
+__device__ __forceinline__ void pair_sync(int id) {
+  asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+__device__ __forceinline__ bool pair_any(int id, bool v) {
+  uint32_t r;
+  asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, 64, p;\n\t"
+               "selp.u32 %0, 1, 0, q;\n\t}"
+               : "=r"(r)
+               : "r"((uint32_t)v), "r"(id)
+               : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, mbar_wait_cluster(bar, parity, kWaitLimitNs));
 }
@@ -162,6 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* kmax_in_s = tmem_base_s + 2;
   float* theta_in = reinterpret_cast<float*>(base + L::off_theta);
   uint32_t* queues = reinterpret_cast<uint32_t*>(base + L::off_queue);
+  int* cnt_s = reinterpret_cast<int*>(base + L::off_cnt);
+  float* thr_s = reinterpret_cast<float*>(base + L::off_thr);
   uint32_t* mkey = reinterpret_cast<uint32_t*>(base + L::off_merge);       // [warp][128]
   int* midx = reinterpret_cast<int*>(mkey + kEpiWarps * 128);              // [warp][128]
 
@@ -186,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&done[s], kEpiWarps);
     }
     mbar_init(qbar, 1);
-    mbar_init(xbar, kM);
+    mbar_init(xbar, 2 * kM);  // both warps of a quadrant post a row's bound
     *kmax_own_s = 0u;
     fence_mbarrier_init();
   }
@@ -267,10 +285,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ============================================================ selection
-    const int r = threadIdx.x;
+    // Two warps per TMEM lane quadrant: warp w owns rows 32*(w%4) .. +31 and the
+    // column half w/4 of every chunk (slices 2*(w/4) and 2*(w/4)+1).
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = 32 * qd + lane;  // query row in the tile = TMEM lane
     const bool row_ok = r < nrows;
     const int g = g0 + r;
-    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    const uint32_t lane_base = (uint32_t)(32 * qd) << 16;
+    const int pair_bar = 1 + qd;   // named barrier of the two warps of this quadrant
     float qabs = 0.f;
     if (row_ok) {
       const TI* qrow = reinterpret_cast<const TI*>(p.q) + (int64_t)b * p.qsb + (int64_t)(l0 + r) * p.qst;
@@ -287,13 +309,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < 32; ++j) ninf[j] = 0xff800000u;
 #pragma unroll
-      for (int blk = 0; blk < kGroups / 32; ++blk) tmem_st_32x32b_x32(tmem_base + lane_base + 256 + blk * 32, ninf);
+      for (int par = 0; par < 2; ++par)
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          tmem_st_32x32b_x32(tmem_base + lane_base + 256 + par * kN + (2 * hf + i) * 32, ninf);
       tmem_st_wait();
+    }
+    if (hf == 0) {
+      cnt_s[r] = 0;
+      thr_s[r] = -INFINITY;
     }
     ok = warp_wait(qbar, 0);
     if (!ok) why |= 64;
 
-    // ---------------- pass 1: group maxima of tensor-core scores
+    // ---------------- pass 1: group maxima of tensor-core scores (this warp's slices)
     for (int w = 0; w < n_own && ok; ++w) {
       const int s = w % S;
       if (!warp_wait(&mdone[s], (uint32_t)(w / S) & 1u)) { ok = false; why |= 128; break; }
@@ -302,7 +331,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc = tmem_base + lane_base + (uint32_t)((w & 1) * kN);
       const uint32_t gcol = tmem_base + lane_base + 256 + (uint32_t)((w & 1) * kN);
 #pragma unroll 1
-      for (int sl = 0; sl < kN / 32; ++sl) {
+      for (int i = 0; i < 2; ++i) {
+        const int sl = 2 * hf + i;
         uint32_t v[32], gm[32];
         tmem_ld_32x32b_x32(acc + sl * 32, v);
         tmem_ld_32x32b_x32(gcol + sl * 32, gm);
@@ -325,8 +355,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&done[s]);
     }
+    // both warps' group maxima (and cnt_s / thr_s) are complete and visible to the pair
+    tmem_st_wait();
+    tc_fence_before();
+    pair_sync(pair_bar);
+    tc_fence_after();
 
-    // ---------------- lower bound on the K-th best score from the group maxima
+    // ---------------- lower bound on the K-th best score from all 256 group maxima
     float theta_own = -INFINITY;
     {
       const uint32_t gbase = tmem_base + lane_base + 256;
@@ -373,8 +408,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // ---------------- exchange bounds and key magnitudes with the peer CTA
+    // (both warps of a quadrant computed the same bound and both post it)
     st_peer_u32(map_peer(&theta_in[r], peer), __float_as_uint(theta_own));
-    if (r == 0) st_peer_u32(map_peer(kmax_in_s, peer), *kmax_own_s);
+    if (r == 0 && hf == 0) st_peer_u32(map_peer(kmax_in_s, peer), *kmax_own_s);
     mbar_arrive_peer(map_peer(xbar, peer));
     if (!warp_wait_cluster(xbar, 0)) { ok = false; why |= 256; }
     const float theta = fmaxf(theta_own, theta_in[r]);
@@ -384,8 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---------------- pass 2: admit, rescore exactly, keep candidates in the workspace
     uint32_t* queue = queues + warp * kQcap;
-    const int64_t row0 = (int64_t)b * p.Tq + l0 + 32 * warp;  // first row of this warp
-    int cnt = 0;
+    const int64_t row0 = (int64_t)b * p.Tq + l0 + 32 * qd;  // first row of this quadrant
     int qsize = 0;  // warp-uniform
 
     auto flush = [&](const unsigned char* stage, int c) {
@@ -393,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int e = lane; e < qsize; e += 32) {
         const uint32_t ent = queue[e];
         const int lr = ent & 31, jj = (ent >> 5) & 127, dest = (int)(ent >> 12);
-        const float ex = dot_swizzled<TI, ROWB>(qs, 32 * warp + lr, stage, jj);
+        const float ex = dot_swizzled<TI, ROWB>(qs, 32 * qd + lr, stage, jj);
         p.ws[((row0 + lr) * 2 + rank) * kWcap + dest] =
             ((uint64_t)ordered_key(ex) << 32) | (uint32_t)(~(uint32_t)(c * kN + jj));
       }
@@ -401,57 +436,77 @@ __global__ void __launch_bounds__(kThreads, 1)
       qsize = 0;
     };
 
-    for (int w = n_own; w < n_work && ok; ++w) {
+    // Every warp runs the same number of rounds (2 per chunk) so the pair
+    // barriers inside stay matched even if a wait of this warp gives up.
+    bool alive = ok;
+    for (int w = n_own; w < n_work; ++w) {
       const int s = w % S;
       const uint32_t ph = (uint32_t)(w / S) & 1u;
-      if (!warp_wait(&mdone[s], ph) || !warp_wait(&full[s], ph)) { ok = false; why |= 512; break; }
+      if (alive && (!warp_wait(&mdone[s], ph) || !warp_wait(&full[s], ph))) {
+        alive = false;
+        ok = false;
+        why |= 512;
+      }
       tc_fence_after();
       const int c = chunk_of(w);
       const unsigned char* stage = ks + s * L::STAGE_STRIDE;
       const uint32_t acc = tmem_base + lane_base + (uint32_t)((w & 1) * kN);
 #pragma unroll 1
-      for (int sl = 0; sl < kN / 32; ++sl) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(acc + sl * 32, v);
-        tmem_ld_wait();
+      for (int i = 0; i < 2; ++i) {
+        const int sl = 2 * hf + i;
         uint32_t m = 0;
+        if (alive) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(acc + sl * 32, v);
+          tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) m |= (__uint_as_float(v[j]) >= lim ? 1u : 0u) << j;
-        const int room = g - (c * kN + sl * 32);
-        if (!row_ok || room < 0) m = 0;
-        else if (room < 31) m &= (2u << room) - 1u;
+          for (int j = 0; j < 32; ++j) m |= (__uint_as_float(v[j]) >= lim ? 1u : 0u) << j;
+          const int room = g - (c * kN + sl * 32);
+          if (!row_ok || room < 0) m = 0;
+          else if (room < 31) m &= (2u << room) - 1u;
+        }
         const int np = __popc(m);
-        // rows whose workspace slice would overflow: rescore what is pending, then
-        // compact them to their exact top-K (rare: about 1.3 K keys per row are admitted)
-        unsigned need = __ballot_sync(kFullMask, cnt + np > kWcap);
-        if (need) {
+        // A round adds at most 64 candidates to a row (32 per warp of the pair).
+        // The vote reads the counter before the partner's last reservation may be
+        // visible (up to 32 more), hence the 96 margin; after the barrier the
+        // counts are exact and rows within 64 of the end are compacted.
+        if (pair_any(pair_bar, row_ok && cnt_s[r] + 96 > kWcap)) {
           flush(stage, c);
-          while (need) {
-            const int ln = __ffs(need) - 1;
-            need &= need - 1;
-            const int n = __shfl_sync(kFullMask, cnt, ln);
-            uint64_t* wrow = p.ws + ((row0 + ln) * 2 + rank) * kWcap;
-            uint32_t kk[kWcap / 32];
-            int ii[kWcap / 32];
+          pair_sync(pair_bar);
+          if (hf == 0) {
+            unsigned need = __ballot_sync(kFullMask, row_ok && cnt_s[r] + 64 > kWcap);
+            while (need) {
+              const int ln = __ffs(need) - 1;
+              need &= need - 1;
+              const int rr = 32 * qd + ln;
+              const int n = cnt_s[rr];
+              uint64_t* wrow = p.ws + ((row0 + ln) * 2 + rank) * kWcap;
+              uint32_t kk[kWcap / 32];
+              int ii[kWcap / 32];
 #pragma unroll
-            for (int t = 0; t < kWcap / 32; ++t) {
-              const int e = t * 32 + lane;
-              const uint64_t cv = e < n ? wrow[e] : 0ull;
-              kk[t] = (uint32_t)(cv >> 32);
-              ii[t] = e < n ? (int)(~(uint32_t)cv) : INT_MAX;
-            }
-            uint32_t* bk = mkey + warp * 128;
-            int* bi = midx + warp * 128;
-            const uint32_t tau = select_compact<kWcap / 32>(kk, ii, n, p.K, lane, bk, bi);
-            for (int e = lane; e < p.K; e += 32) wrow[e] = ((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e]);
-            __syncwarp();
-            if (lane == ln) {
-              cnt = p.K;
-              lim = fmaxf(lim, key_to_float(tau) - eps);
+              for (int t = 0; t < kWcap / 32; ++t) {
+                const int e = t * 32 + lane;
+                const uint64_t cv = e < n ? wrow[e] : 0ull;
+                kk[t] = (uint32_t)(cv >> 32);
+                ii[t] = e < n ? (int)(~(uint32_t)cv) : INT_MAX;
+              }
+              uint32_t* bk = mkey + qd * 128;
+              int* bi = midx + qd * 128;
+              const uint32_t tau = select_compact<kWcap / 32>(kk, ii, n, p.K, lane, bk, bi);
+              for (int e = lane; e < p.K; e += 32) wrow[e] = ((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e]);
+              __syncwarp();
+              if (lane == 0) {
+                cnt_s[rr] = p.K;
+                thr_s[rr] = key_to_float(tau);
+              }
+              __syncwarp();
             }
           }
+          pair_sync(pair_bar);
+          lim = fmaxf(lim, thr_s[r] - eps);
         }
-        // queue the admitted (row, key) pairs with their workspace slots
+        // reserve workspace slots for this warp's admitted keys of the row
+        const int base = np ? atomicAdd(&cnt_s[r], np) : 0;
         int incl = np;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -465,10 +520,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         while (m) {
           const int j = __ffs(m) - 1;
           m &= m - 1;
-          queue[pos + k] = (uint32_t)lane | ((uint32_t)(sl * 32 + j) << 5) | ((uint32_t)(cnt + k) << 12);
+          queue[pos + k] = (uint32_t)lane | ((uint32_t)(sl * 32 + j) << 5) | ((uint32_t)(base + k) << 12);
           ++k;
         }
-        cnt += np;
         qsize += total;
       }
       flush(stage, c);  // the stage is about to be released
@@ -476,7 +530,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&done[s]);
     }
-    if (row_ok) p.ws_cnt[(row0 + lane) * 2 + rank] = cnt;
+    pair_sync(pair_bar);
+    if (hf == 0 && row_ok) p.ws_cnt[(row0 + lane) * 2 + rank] = cnt_s[r];
   }
   if (!ok && p.status) atomicOr(p.status, 2 | (int)why);
 

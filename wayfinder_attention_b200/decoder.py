@@ -19,7 +19,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .attention import LearnedAddressSparseAttention
+from .attention import KeyVectorSparseAttention, LearnedAddressSparseAttention
 
 
 class DenseSDPAAttention(nn.Module):
@@ -81,7 +81,7 @@ class TransformerLM(nn.Module):
         pad_token_id: int = 0,
     ):
         super().__init__()
-        if attention_type not in ("learned_address", "dense_flash", "dense"):
+        if attention_type not in ("learned_address", "key_vector", "dense_flash", "dense"):
             raise ValueError(f"attention_type {attention_type!r} is outside this build's scope")
         self.d_model = d_model
         self.max_seq_len = max_seq_len
@@ -96,6 +96,9 @@ class TransformerLM(nn.Module):
                     d_model, n_heads, routing_top_k, address_dim=address_dim, dropout=dropout,
                     retrieval_config=retrieval_config,
                 )
+            elif attention_type == "key_vector":
+                attn = KeyVectorSparseAttention(d_model, n_heads, routing_top_k, dropout=dropout,
+                                                retrieval_config=retrieval_config)
             else:
                 attn = DenseSDPAAttention(d_model, n_heads, dropout)
             self.blocks.append(TransformerBlock(d_model, n_heads, d_ff, dropout, attn, layer_idx=i))
