@@ -195,6 +195,7 @@ def main() -> None:
     ap.add_argument("--cpu-baseline-rows", type=int, default=16384, help="rows of the one-off cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-dense", action="store_true")
+    ap.add_argument("--no-decoder", action="store_true", help="skip the whole-decoder prefill measurements")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -356,6 +357,15 @@ def main() -> None:
         }
         if not args.no_dense:
             result["dense_sdpa"] = dense_baseline(w, x, flush, args.steps)
+        if not args.no_decoder and args.config == "cfg2":
+            # the reference publishes this model's forward latency (B=1, T=16384: 38.35 ms on an RTX 5090,
+            # fp32 + TF32; dense flash 84.33 ms), and cfg3 is the same family at B=8, T=4096
+            result["decoder_prefill"] = {
+                "systems_T16384": decoder_forward(1, 16384, flush, 5, dev),
+                "systems_T16384_dense": decoder_forward(1, 16384, flush, 5, dev, attention_type="dense_flash"),
+                "cfg3_B8_T4096": decoder_forward(8, 4096, flush, 5, dev),
+                "published_rtx5090_ms": {"wayfinder_T16384": 38.35, "dense_flash_T16384": 84.33},
+            }
         if world == 1 and not args.no_cpu_baseline:
             secs, n = time_cpu_oracle(w, host, args.cpu_baseline_rows)
             result["cpu_baseline"] = {
@@ -427,6 +437,36 @@ def run_sequence_sharded(args, w: Workload, rank: int, world: int, dev) -> None:
             "gpu_launches": 3 * args.steps,  # per step: retrieval, finalisation, attention
             "clocks": clk.summary(),
         }), flush=True)
+
+
+def decoder_forward(B: int, T: int, flush: torch.Tensor, steps: int, dev, attention_type: str = "learned_address") -> dict:
+    """Whole-model prefill forward of the reference's systems-benchmark model family
+    (4 layers, d_model 256, 4 heads, FFN 1024, vocab 128, K 128; transformer.py:76-312)
+    with this build's attention, bf16 weights, random init, uniform token ids."""
+    from wayfinder_attention_b200 import TransformerLM
+
+    torch.manual_seed(45)
+    m = TransformerLM(128, d_model=256, n_layers=4, n_heads=4, d_ff=1024, max_seq_len=T, dropout=0.0,
+                      attention_type=attention_type, routing_top_k=128,
+                      retrieval_config={"use_fused_sparse": True, "method": "fused_causal"})
+    m = m.to(dev, torch.bfloat16).eval()
+    ids = torch.randint(0, 128, (B, T), device=dev, generator=torch.Generator(device=dev).manual_seed(45))
+    with torch.no_grad():
+        for _ in range(3):
+            m(ids)
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            m(ids)
+            b.record()
+            torch.cuda.synchronize()
+            tot += a.elapsed_time(b)
+    ms = tot / steps
+    return {"ms": ms, "tokens_per_s": B * T / (ms / 1e3), "B": B, "T": T, "attention": attention_type,
+            "model": "4 layers, d_model 256, H 4, FFN 1024, vocab 128, K 128, bf16"}
 
 
 def dense_baseline(w: Workload, x: dict, flush: torch.Tensor, steps: int) -> dict:
