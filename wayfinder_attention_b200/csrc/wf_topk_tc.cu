@@ -330,25 +330,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int c = chunk_of(w);
       const uint32_t acc = tmem_base + lane_base + (uint32_t)((w & 1) * kN);
       const uint32_t gcol = tmem_base + lane_base + 256 + (uint32_t)((w & 1) * kN);
-#pragma unroll 1
-      for (int i = 0; i < 2; ++i) {
-        const int sl = 2 * hf + i;
-        uint32_t v[32], gm[32];
-        tmem_ld_32x32b_x32(acc + sl * 32, v);
-        tmem_ld_32x32b_x32(gcol + sl * 32, gm);
-        tmem_ld_wait();
-        const int room = g - (c * kN + sl * 32);
-        if (row_ok && room >= 31) {
+      {
+        // both of this warp's slices in flight before a single wait
+        uint32_t v[2][32], gm[2][32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) gm[j] = __float_as_uint(fmaxf(__uint_as_float(gm[j]), __uint_as_float(v[j])));
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float x = (row_ok && j <= room) ? __uint_as_float(v[j]) : -INFINITY;
-            gm[j] = __float_as_uint(fmaxf(__uint_as_float(gm[j]), x));
-          }
+        for (int i = 0; i < 2; ++i) {
+          tmem_ld_32x32b_x32(acc + (2 * hf + i) * 32, v[i]);
+          tmem_ld_32x32b_x32(gcol + (2 * hf + i) * 32, gm[i]);
         }
-        tmem_st_32x32b_x32(gcol + sl * 32, gm);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int sl = 2 * hf + i;
+          const int room = g - (c * kN + sl * 32);
+          if (row_ok && room >= 31) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              gm[i][j] = __float_as_uint(fmaxf(__uint_as_float(gm[i][j]), __uint_as_float(v[i][j])));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float x = (row_ok && j <= room) ? __uint_as_float(v[i][j]) : -INFINITY;
+              gm[i][j] = __float_as_uint(fmaxf(__uint_as_float(gm[i][j]), x));
+            }
+          }
+          tmem_st_32x32b_x32(gcol + sl * 32, gm[i]);
+        }
       }
       tmem_st_wait();
       tc_fence_before();
@@ -451,20 +458,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int c = chunk_of(w);
       const unsigned char* stage = ks + s * L::STAGE_STRIDE;
       const uint32_t acc = tmem_base + lane_base + (uint32_t)((w & 1) * kN);
+      // admission masks of both slices (loads in flight together)
+      uint32_t masks[2] = {0u, 0u};
+      if (alive) {
+        uint32_t v[2][32];
+        tmem_ld_32x32b_x32(acc + (2 * hf) * 32, v[0]);
+        tmem_ld_32x32b_x32(acc + (2 * hf + 1) * 32, v[1]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          uint32_t m = 0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) m |= (__uint_as_float(v[i][j]) >= lim ? 1u : 0u) << j;
+          const int room = g - (c * kN + (2 * hf + i) * 32);
+          if (!row_ok || room < 0) m = 0;
+          else if (room < 31) m &= (2u << room) - 1u;
+          masks[i] = m;
+        }
+      }
 #pragma unroll 1
       for (int i = 0; i < 2; ++i) {
         const int sl = 2 * hf + i;
-        uint32_t m = 0;
-        if (alive) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(acc + sl * 32, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) m |= (__uint_as_float(v[j]) >= lim ? 1u : 0u) << j;
-          const int room = g - (c * kN + sl * 32);
-          if (!row_ok || room < 0) m = 0;
-          else if (room < 31) m &= (2u << room) - 1u;
-        }
+        uint32_t m = masks[i];
         const int np = __popc(m);
         // A round adds at most 64 candidates to a row (32 per warp of the pair).
         // The vote reads the counter before the partner's last reservation may be
