@@ -54,6 +54,26 @@ def load_peaks() -> tuple[dict, str]:
     return dict(FALLBACK_PEAKS), "fallback"
 
 
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Write the one JSON result line to the process's real stdout."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
+def claim_stdout() -> None:
+    """Route fd 1 to stderr so library banners (NCCL prints its version on stdout)
+    cannot interleave with the JSON line, which goes to a private copy of stdout."""
+    global _JSON_OUT
+    if _JSON_OUT is None:
+        sys.stdout.flush()
+        _JSON_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
 def dist_env() -> tuple[int, int, int]:
     return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
 
@@ -181,7 +201,7 @@ def run_reference_arm(args, w: Workload) -> None:
                                    f"(retrieval over their causal prefixes + attention over {w.H} heads)"},
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def main() -> None:
@@ -198,6 +218,7 @@ def main() -> None:
     ap.add_argument("--no-decoder", action="store_true", help="skip the whole-decoder prefill measurements")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    claim_stdout()
 
     w = CONFIGS[args.config]
     if args.impl == "reference":
@@ -378,7 +399,7 @@ def main() -> None:
         dist.barrier()
         dist.destroy_process_group()
     if result is not None:
-        print(json.dumps(result), flush=True)
+        emit(result)
 
 
 def run_sequence_sharded(args, w: Workload, rank: int, world: int, dev) -> None:
@@ -425,7 +446,7 @@ def run_sequence_sharded(args, w: Workload, rank: int, world: int, dev) -> None:
         peaks, peak_kind = load_peaks()
         roof_ms = 1e3 * max(w.score_flops() / (float(peaks["bf16_tflops"]) * 1e12),
                             w.gathered_bytes() / (float(peaks["hbm_gbs"]) * 1e9)) / world
-        print(json.dumps({
+        emit({
             "metric": METRIC, "value": w.B * w.T / (ms / 1e3), "unit": "queries/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, generated on device)",
@@ -436,7 +457,7 @@ def run_sequence_sharded(args, w: Workload, rank: int, world: int, dev) -> None:
             "path_roofline": {"roofline_ms_per_gpu": roof_ms, "frac": roof_ms / ms, "peak_kind": peak_kind},
             "gpu_launches": 3 * args.steps,  # per step: retrieval, finalisation, attention
             "clocks": clk.summary(),
-        }), flush=True)
+        })
 
 
 def decoder_forward(B: int, T: int, flush: torch.Tensor, steps: int, dev, attention_type: str = "learned_address") -> dict:
