@@ -136,6 +136,25 @@ WF_API int wf_sparse_attention(const void* q, const void* k, const void* v, int3
                         int32_t* status, void* stream);
 
 /*
+ * wf_sparse_attention for one long sequence split over ranks in cyclic row blocks
+ * (the query-row sharding of the multi-GPU path) whose K/V were all-gathered
+ * rank-major, so no reordering copy is needed.  It has no counterpart in the
+ * reference, which is single-GPU.  Keys are addressed by their global position j:
+ * j lives on rank (j / kv_row_tile) % kv_world at local row
+ * (j / kv_row_tile / kv_world) * kv_row_tile + j % kv_row_tile.  k and v point at
+ * rank 0's block, k_strides / v_strides describe one rank's (B, H, Tk / kv_world, D)
+ * block and k_rank_stride / v_rank_stride (elements) step from one rank to the next.
+ */
+WF_API int wf_sparse_attention_cyclic_kv(const void* q, const void* k, const void* v, int32_t dtype,
+                                         const int32_t* idx, int64_t B, int64_t H, int64_t Tq, int64_t Tk,
+                                         int32_t D, int32_t K, const int64_t* q_strides,
+                                         const int64_t* k_strides, const int64_t* v_strides,
+                                         const int64_t* idx_strides, float scale, int32_t flags, void* out,
+                                         int32_t out_dtype, const int64_t* out_strides, int32_t kv_row_tile,
+                                         int32_t kv_world, int64_t k_rank_stride, int64_t v_rank_stride,
+                                         int32_t* status, void* stream);
+
+/*
  * Retrieval + attention in one call.  Replaces fused_sparse_attention()
  * (routing_attention/kernels/fused_sparse.py:327-356): wf_causal_topk into idx_out,
  * then wf_sparse_attention over it (masking pads when pad_mode == WF_PAD_MASKED).

@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "wf_causal_topk_workspace_bytes",
     "wf_causal_topk",
     "wf_sparse_attention",
+    "wf_sparse_attention_cyclic_kv",
     "wf_fused_sparse_attention",
 )
 
@@ -75,6 +76,11 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.wf_sparse_attention.argtypes = [
         _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i32, _i32,
         _i64p, _i64p, _i64p, _i64p, _f32, _i32, _vp, _i32, _i64p, _vp, _vp,
+    ]
+    lib.wf_sparse_attention_cyclic_kv.restype = ctypes.c_int
+    lib.wf_sparse_attention_cyclic_kv.argtypes = [
+        _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i32, _i32,
+        _i64p, _i64p, _i64p, _i64p, _f32, _i32, _vp, _i32, _i64p, _i32, _i32, _i64, _i64, _vp, _vp,
     ]
     lib.wf_fused_sparse_attention.restype = ctypes.c_int
     lib.wf_fused_sparse_attention.argtypes = [

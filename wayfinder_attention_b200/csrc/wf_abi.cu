@@ -171,11 +171,12 @@ int wf_causal_topk(const void* q_addr, const void* k_addr, int32_t dtype, int64_
   return ok();
 }
 
-int wf_sparse_attention(const void* q, const void* k, const void* v, int32_t dtype, const int32_t* idx,
-                        int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t D, int32_t K,
-                        const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
-                        const int64_t* idx_strides, float scale, int32_t flags, void* out, int32_t out_dtype,
-                        const int64_t* out_strides, int32_t* status, void* stream) {
+namespace {
+int attention_impl(const void* q, const void* k, const void* v, int32_t dtype, const int32_t* idx, int64_t B,
+                   int64_t H, int64_t Tq, int64_t Tk, int32_t D, int32_t K, const int64_t* q_strides,
+                   const int64_t* k_strides, const int64_t* v_strides, const int64_t* idx_strides, float scale,
+                   int32_t flags, void* out, int32_t out_dtype, const int64_t* out_strides, int32_t* status,
+                   void* stream, int32_t kv_tile, int32_t kv_world, int64_t k_rank_stride, int64_t v_rank_stride) {
   int rc = check_attn(q, k, v, dtype, idx, B, H, Tq, Tk, D, K, q_strides, k_strides, v_strides, idx_strides,
                       scale, flags, out, out_dtype, out_strides);
   if (rc) return rc;
@@ -191,6 +192,10 @@ int wf_sparse_attention(const void* q, const void* k, const void* v, int32_t dty
   p.scale = scale;
   p.mask_negative = (flags & WF_ATTN_MASK_NEGATIVE) ? 1 : 0;
   p.status = status;
+  p.kv_tile = kv_tile;
+  p.kv_world = kv_world;
+  p.k_rank_stride = k_rank_stride;
+  p.v_rank_stride = v_rank_stride;
   {
     const int osz = dtype_size(out_dtype);
     p.out_vec_ok = (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (out_strides[0] * osz) % 16 == 0 &&
@@ -199,6 +204,37 @@ int wf_sparse_attention(const void* q, const void* k, const void* v, int32_t dty
   rc = wf::launch_sparse_attention(p, dtype, out_dtype, static_cast<cudaStream_t>(stream));
   if (rc) return cuda_fail(rc, "wf_sparse_attention");
   return ok();
+}
+}  // namespace
+
+int wf_sparse_attention(const void* q, const void* k, const void* v, int32_t dtype, const int32_t* idx,
+                        int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t D, int32_t K,
+                        const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                        const int64_t* idx_strides, float scale, int32_t flags, void* out, int32_t out_dtype,
+                        const int64_t* out_strides, int32_t* status, void* stream) {
+  return attention_impl(q, k, v, dtype, idx, B, H, Tq, Tk, D, K, q_strides, k_strides, v_strides, idx_strides,
+                        scale, flags, out, out_dtype, out_strides, status, stream, 0, 1, 0, 0);
+}
+
+int wf_sparse_attention_cyclic_kv(const void* q, const void* k, const void* v, int32_t dtype, const int32_t* idx,
+                                  int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t D, int32_t K,
+                                  const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                                  const int64_t* idx_strides, float scale, int32_t flags, void* out,
+                                  int32_t out_dtype, const int64_t* out_strides, int32_t kv_row_tile,
+                                  int32_t kv_world, int64_t k_rank_stride, int64_t v_rank_stride,
+                                  int32_t* status, void* stream) {
+  if (kv_world < 1 || kv_world > 64) return fail(WF_ERR_INVALID_ARGUMENT, "kv_world must be in [1, 64], got %d", kv_world);
+  if (kv_row_tile < 1) return fail(WF_ERR_INVALID_ARGUMENT, "kv_row_tile must be >= 1, got %d", kv_row_tile);
+  if (Tk >= (int64_t(1) << 25)) return fail(WF_ERR_UNSUPPORTED, "Tk=%lld too large for the rank-major key layout", (long long)Tk);
+  if (Tk % ((int64_t)kv_row_tile * kv_world))
+    return fail(WF_ERR_INVALID_ARGUMENT, "Tk=%lld is not a whole number of %d-row blocks on %d ranks", (long long)Tk,
+                kv_row_tile, kv_world);
+  const int esz = dtype_size(dtype);
+  if ((k_rank_stride * esz) % 16 || (v_rank_stride * esz) % 16)
+    return fail(WF_ERR_UNSUPPORTED, "rank strides must be multiples of 16 bytes");
+  return attention_impl(q, k, v, dtype, idx, B, H, Tq, Tk, D, K, q_strides, k_strides, v_strides, idx_strides,
+                        scale, flags, out, out_dtype, out_strides, status, stream, kv_row_tile, kv_world,
+                        k_rank_stride, v_rank_stride);
 }
 
 int wf_fused_sparse_attention(const void* q_addr, const void* k_addr, int32_t addr_dtype, int32_t R,

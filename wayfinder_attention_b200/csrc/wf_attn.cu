@@ -60,6 +60,12 @@ __device__ __forceinline__ void store_vec<float>(float* o, const float* v, int n
   for (int i = 0; i < n; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
 }
 
+// Element offset of decoded key slot j (see the decode step) for row stride st.
+__device__ __forceinline__ int64_t kv_row_offset(const AttnParams& p, int j, int64_t st, int64_t rank_stride) {
+  if (p.kv_world <= 1) return (int64_t)j * st;
+  return (int64_t)(j >> 25) * rank_stride + (int64_t)(j & ((1 << 25) - 1)) * st;
+}
+
 template <typename TI, typename TO, int D, int E>
 __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, int warps_per_block) {
   using V16 = Vec16<TI>;
@@ -101,6 +107,12 @@ __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, in
       j = kBad;
       bad = true;
     }
+    if (j >= 0 && p.kv_world > 1) {
+      // rank-major gathered keys: rank r's rows follow each other, r < kv_world <= 64,
+      // stored as r * 2^25 + local row (Tk < 2^25 is checked by the caller)
+      const int blk = j / p.kv_tile;
+      j = ((blk % p.kv_world) << 25) | ((blk / p.kv_world) * p.kv_tile + j % p.kv_tile);
+    }
     sI[s] = j;
   }
   if (__any_sync(kFull, bad) && lane == 0 && p.status) atomicOr(p.status, 1);
@@ -131,7 +143,7 @@ __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, in
       jj[u] = j;
 #pragma unroll
       for (int v = 0; v < NV; ++v)
-        raw[u][v] = (j >= 0 && hv) ? ldg16(kb + (int64_t)j * p.kst + v * L * VEC) : make_uint4(0, 0, 0, 0);
+        raw[u][v] = (j >= 0 && hv) ? ldg16(kb + kv_row_offset(p, j, p.kst, p.k_rank_stride) + v * L * VEC) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
@@ -185,7 +197,7 @@ __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, in
       pw[u] = in ? myP[k0 + u] : 0.f;
 #pragma unroll
       for (int v = 0; v < NV; ++v)
-        raw[u][v] = (j >= 0 && hv) ? ldg16(vb + (int64_t)j * p.vst + v * L * VEC) : make_uint4(0, 0, 0, 0);
+        raw[u][v] = (j >= 0 && hv) ? ldg16(vb + kv_row_offset(p, j, p.vst, p.v_rank_stride) + v * L * VEC) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < kU; ++u) {

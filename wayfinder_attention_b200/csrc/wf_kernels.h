@@ -43,6 +43,11 @@ struct AttnParams {
   float scale;
   int mask_negative;     // 1: negative index = masked slot; 0: wraps like torch indexing
   int out_vec_ok;        // output rows are 16-byte aligned (vector stores allowed)
+  // Keys of a sequence sharded in cyclic row blocks and all-gathered rank-major:
+  // key j lives in rank (j / kv_tile) % kv_world at local row
+  // (j / kv_tile / kv_world) * kv_tile + j % kv_tile.  kv_world = 1: identity.
+  int kv_tile, kv_world;
+  int64_t k_rank_stride, v_rank_stride;
   int32_t* status;       // nullable; bit 0 set on an out-of-range index
 };
 

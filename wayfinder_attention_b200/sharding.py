@@ -60,12 +60,14 @@ def sharded_causal_topk(q_addr_local: torch.Tensor, k_addr_full: torch.Tensor, t
     return _launch_topk(q, k, top_k, pad_mode, row_tile=tile, row_stride=world, row_start=rank)
 
 
-def _all_gather_rows(x_local: torch.Tensor, world: int, group=None) -> torch.Tensor:
+def _all_gather_rows(x_local: torch.Tensor, world: int, group=None, out: torch.Tensor | None = None) -> torch.Tensor:
     """All-gather (B, Tl, ...) shards along dim 1 into a rank-major (world, B, Tl, ...) tensor."""
     import torch.distributed as dist
 
     x_local = x_local.contiguous()
-    out = torch.empty((world,) + tuple(x_local.shape), dtype=x_local.dtype, device=x_local.device)
+    shape = (world,) + tuple(x_local.shape)
+    if out is None or tuple(out.shape) != shape or out.dtype != x_local.dtype or out.device != x_local.device:
+        out = torch.empty(shape, dtype=x_local.dtype, device=x_local.device)
     if dist.get_backend(group) == "nccl":
         dist.all_gather_into_tensor(out, x_local, group=group)
     else:
@@ -107,6 +109,8 @@ class SequenceShardedAttention:
       2. runs the causal top-K of its own rows against all keys (row map of
          ``wf_causal_topk``) while K/V are in flight;
       3. waits for K/V and runs the sparse attention of its rows.
+    The K/V all-gathers land rank-major and the attention kernel translates key
+    positions to (rank, local row) itself, so no reordering copy of K/V is made.
     The only collectives are these all-gathers; nothing crosses ranks afterwards.
     """
 
@@ -116,32 +120,49 @@ class SequenceShardedAttention:
         self.tile = tile
         self.group = group
         self.pad_mode = pad_mode
+        # persistent per-shape gather buffers and side stream: a forward allocates nothing large
+        self._kg = None
+        self._vg = None
+        self._side = None
 
     def forward(self, q_addr_l: torch.Tensor, k_addr_l: torch.Tensor, q_l: torch.Tensor, k_l: torch.Tensor,
                 v_l: torch.Tensor, out_dtype: torch.dtype | None = None) -> tuple[torch.Tensor, torch.Tensor]:
         """q_addr_l, k_addr_l: (B, Tl, R); q_l, k_l, v_l: (B, H, Tl, D) views of (B, Tl, H, D) memory."""
         import torch.distributed as dist
 
-        from .fused_sparse import _launch_attention
+        from . import _lib
 
         world = dist.get_world_size(self.group)
         rank = dist.get_rank(self.group)
         B, H, Tl, D = q_l.shape
         T = world * Tl
         main = torch.cuda.current_stream(q_l.device)
-        side = torch.cuda.Stream(device=q_l.device)
-        side.wait_stream(main)
+        if self._side is None or self._side.device != q_l.device:
+            self._side = torch.cuda.Stream(device=q_l.device)
+        side = self._side
+        side.wait_stream(main)  # the previous call's attention has finished with the buffers
         with torch.cuda.stream(side):
-            k_full = gather_sequence(k_l.transpose(1, 2), self.tile, self.group).transpose(1, 2)
-            v_full = gather_sequence(v_l.transpose(1, 2), self.tile, self.group).transpose(1, 2)
-        k_addr = gather_sequence(k_addr_l, self.tile, self.group)
+            # rank-major (world, B, Tl, H, D): the attention kernel addresses it directly
+            self._kg = k_g = _all_gather_rows(k_l.transpose(1, 2), world, self.group, self._kg)
+            self._vg = v_g = _all_gather_rows(v_l.transpose(1, 2), world, self.group, self._vg)
+        k_addr = gather_sequence(k_addr_l, self.tile, self.group)  # small: reordered to global order
         idx = sharded_causal_topk(q_addr_l, k_addr, self.top_k, world, rank, self.tile, self.pad_mode)
         main.wait_stream(side)
-        k_full.record_stream(main)
-        v_full.record_stream(main)
-        out = _launch_attention(q_l, k_full, v_full, idx, self.scale, mask_negative=self.pad_mode == "masked",
-                                out_dtype=out_dtype)
-        assert k_full.shape[2] == T
+        dev = q_l.device
+        out = torch.empty(B, H, Tl, D, dtype=out_dtype or q_l.dtype, device=dev)
+        kb = k_g[0].transpose(1, 2)  # rank 0's block as (B, H, Tl, D)
+        vb = v_g[0].transpose(1, 2)
+        K = idx.shape[-1]
+        lib = _lib.load_library()
+        with torch.cuda.device(dev):
+            rc = lib.wf_sparse_attention_cyclic_kv(
+                q_l.data_ptr(), kb.data_ptr(), vb.data_ptr(), _lib.dtype_code(q_l.dtype), idx.data_ptr(),
+                B, H, Tl, T, D, K, _lib.strides(q_l), _lib.strides(kb), _lib.strides(vb), _lib.strides(idx),
+                float(self.scale), _lib.WF_ATTN_MASK_NEGATIVE if self.pad_mode == "masked" else 0,
+                out.data_ptr(), _lib.dtype_code(out.dtype), _lib.strides(out), self.tile, world,
+                k_g.stride(0), v_g.stride(0), None, _lib.stream_ptr(dev),
+            )
+        _lib.check(rc)
         return out, idx
 
     __call__ = forward
