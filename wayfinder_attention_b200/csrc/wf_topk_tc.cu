@@ -83,6 +83,8 @@ struct TcParams {
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+constexpr int kXRounds = 11;  // pair exchanges for the bound: extrema + 10 bisection steps
+
 template <int R, int EPL>
 struct Layout {
   static constexpr int ROWB = R * 2;
@@ -94,12 +96,12 @@ struct Layout {
   static constexpr size_t off_k = align_up(Q_BYTES, 1024);
   static constexpr size_t off_kmax = off_k + S * STAGE_STRIDE;
   static constexpr size_t off_bar = align_up(off_kmax + sizeof(float) * S, 8);
-  static constexpr size_t n_bar = 3 * S + 2;  // full, mdone, done, qbar, xbar
+  static constexpr size_t n_bar = 3 * S + 2 + kXRounds;  // full, mdone, done, qbar, kbar, xbar[rounds]
   static constexpr size_t off_misc = off_bar + 8 * n_bar;  // tmem base, kmax own, kmax peer, abort
-  static constexpr size_t off_theta = align_up(off_misc + 16, 16);
-  static constexpr size_t off_cnt = off_theta + 4 * kM;   // per-row workspace slot counters
+  static constexpr size_t off_cnt = align_up(off_misc + 16, 16);   // per-row workspace slot counters
   static constexpr size_t off_thr = off_cnt + 4 * kM;     // per-row thresholds after a compaction
-  static constexpr size_t off_queue = off_thr + 4 * kM;
+  static constexpr size_t off_xslot = off_thr + 4 * kM;  // [2 parities][kM rows][4] bisection exchange
+  static constexpr size_t off_queue = off_xslot + 4 * 2 * kM * 4;
   static constexpr size_t off_merge = off_queue + 4 * (size_t)kQcap * kEpiWarps;  // per warp: K keys + K indices
   static constexpr size_t bytes = off_merge + (size_t)kEpiWarps * 128 * (4 + 4);
   // Slack to align the dynamic base to 1024, and at least 116 KB in total: two of
@@ -172,13 +174,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* mdone = full + S;
   uint64_t* done = mdone + S;
   uint64_t* qbar = done + S;
-  uint64_t* xbar = qbar + 1;  // peer posted its pass-1 bound
+  uint64_t* kbar = qbar + 1;  // peer posted its key magnitude
+  // One single-use barrier per bisection exchange: a fast warp of the peer may post
+  // step i+1 before a slow one has posted step i, so the steps cannot share phases.
+  uint64_t* xbar = qbar + 2;
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(base + L::off_misc);
   uint32_t* kmax_own_s = tmem_base_s + 1;
   uint32_t* kmax_in_s = tmem_base_s + 2;
-  float* theta_in = reinterpret_cast<float*>(base + L::off_theta);
   uint32_t* queues = reinterpret_cast<uint32_t*>(base + L::off_queue);
   int* cnt_s = reinterpret_cast<int*>(base + L::off_cnt);
+  uint32_t* xslot = reinterpret_cast<uint32_t*>(base + L::off_xslot);
   float* thr_s = reinterpret_cast<float*>(base + L::off_thr);
   uint32_t* mkey = reinterpret_cast<uint32_t*>(base + L::off_merge);       // [warp][128]
   int* midx = reinterpret_cast<int*>(mkey + kEpiWarps * 128);              // [warp][128]
@@ -204,7 +209,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&done[s], kEpiWarps);
     }
     mbar_init(qbar, 1);
-    mbar_init(xbar, 2 * kM);  // both warps of a quadrant post a row's bound
+    for (int i = 0; i < kXRounds; ++i) mbar_init(&xbar[i], 2 * kM);  // both warps of a quadrant post a row
+    mbar_init(kbar, 2 * kM);
     *kmax_own_s = 0u;
     fence_mbarrier_init();
   }
@@ -368,59 +374,73 @@ __global__ void __launch_bounds__(kThreads, 1)
     pair_sync(pair_bar);
     tc_fence_after();
 
-    // ---------------- lower bound on the K-th best score from all 256 group maxima
-    float theta_own = -INFINITY;
-    {
-      const uint32_t gbase = tmem_base + lane_base + 256;
-      int nf = 0;
-      float mn = INFINITY, mx = -INFINITY;
+    // ---------------- lower bound on the K-th best score from the pair's 512 group maxima
+    // Both CTAs bisect the same value range over the union of their maxima: each
+    // step counts its own maxima >= mid, swaps the count with the peer thread of the
+    // same row through DSMEM (remote store + remote mbarrier arrive), and applies
+    // the same decision, so both end with the same bound.  The K-th largest of the
+    // union is the score of K distinct keys, so it lower-bounds the row's K-th score.
+    const uint32_t gbase = tmem_base + lane_base + 256;
+    int nf = 0;
+    float mn = INFINITY, mx = -INFINITY;
+#pragma unroll 1
+    for (int blk = 0; blk < kGroups / 32; ++blk) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(gbase + blk * 32, v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float x = __uint_as_float(v[j]);
+        if (x > -INFINITY) {
+          ++nf;
+          mn = fminf(mn, x);
+          mx = fmaxf(mx, x);
+        }
+      }
+    }
+    // one exchange round: send (a, b, c) to the peer thread of this row, receive its triple
+    auto swap3 = [&](int round, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t (&got)[3]) {
+      uint32_t* slot = xslot + ((round & 1) * kM + r) * 4;
+      const uint32_t peer_slot = map_peer(slot, peer);
+      st_peer_u32(peer_slot, a0);
+      st_peer_u32(peer_slot + 4, a1);
+      st_peer_u32(peer_slot + 8, a2);
+      mbar_arrive_peer(map_peer(&xbar[round], peer));
+      if (!warp_wait_cluster(&xbar[round], 0)) { ok = false; why |= 256; }
+      got[0] = slot[0];
+      got[1] = slot[1];
+      got[2] = slot[2];
+    };
+    uint32_t got[3];
+    swap3(0, (uint32_t)nf, __float_as_uint(mn), __float_as_uint(mx), got);
+    const int nf_t = nf + (int)got[0];
+    float lo = fminf(mn, __uint_as_float(got[1])), hi = fmaxf(mx, __uint_as_float(got[2]));
+    const bool bis = nf_t >= p.K;
+    if (!bis) lo = hi = 0.f;
+    // every thread runs every step (tcgen05.ld is warp-collective and every step is
+    // an exchange the peer waits for); rows with fewer than K maxima ignore the result
+#pragma unroll 1
+    for (int it = 0; it < kXRounds - 1; ++it) {
+      const float mid = lo + 0.5f * (hi - lo);
+      int c = 0;
 #pragma unroll 1
       for (int blk = 0; blk < kGroups / 32; ++blk) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(gbase + blk * 32, v);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float x = __uint_as_float(v[j]);
-          if (x > -INFINITY) {
-            ++nf;
-            mn = fminf(mn, x);
-            mx = fmaxf(mx, x);
-          }
-        }
+        for (int j = 0; j < 32; ++j) c += __uint_as_float(v[j]) >= mid ? 1 : 0;
       }
-      // tcgen05.ld is warp-collective: every lane runs the bisection, only lanes
-      // with at least K finite maxima keep its result.
-      const bool bis = nf >= p.K;
-      if (__any_sync(kFullMask, bis)) {
-        // largest lo with #(maxima >= lo) >= K, to within (mx - mn) / 2^10
-        float lo = bis ? mn : 0.f, hi = bis ? mx : 0.f;
-#pragma unroll 1
-        for (int it = 0; it < 10; ++it) {
-          const float mid = lo + 0.5f * (hi - lo);
-          int c = 0;
-#pragma unroll 1
-          for (int blk = 0; blk < kGroups / 32; ++blk) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(gbase + blk * 32, v);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) c += __uint_as_float(v[j]) >= mid ? 1 : 0;
-          }
-          if (c >= p.K) lo = mid;
-          else hi = mid;
-        }
-        if (bis) theta_own = lo;
-      }
+      swap3(1 + it, (uint32_t)c, 0u, 0u, got);
+      if (c + (int)got[0] >= p.K) lo = mid;
+      else hi = mid;
     }
+    const float theta = bis ? lo : -INFINITY;
 
-    // ---------------- exchange bounds and key magnitudes with the peer CTA
-    // (both warps of a quadrant computed the same bound and both post it)
-    st_peer_u32(map_peer(&theta_in[r], peer), __float_as_uint(theta_own));
+    // key magnitudes for the margin: the peer's arrives with the first exchange
     if (r == 0 && hf == 0) st_peer_u32(map_peer(kmax_in_s, peer), *kmax_own_s);
-    mbar_arrive_peer(map_peer(xbar, peer));
-    if (!warp_wait_cluster(xbar, 0)) { ok = false; why |= 256; }
-    const float theta = fmaxf(theta_own, theta_in[r]);
+    mbar_arrive_peer(map_peer(kbar, peer));
+    if (!warp_wait_cluster(kbar, 0)) { ok = false; why |= 1024; }
     const float kpair = fmaxf(__uint_as_float(*kmax_own_s), __uint_as_float(*kmax_in_s));
     const float eps = kEpsScale * qabs * kpair;
     float lim = theta > -INFINITY ? theta - eps : -INFINITY;
