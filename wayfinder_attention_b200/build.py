@@ -22,7 +22,8 @@ CSRC = PKG_DIR / "csrc"
 LIB_NAME = "libwayfinder_sm100.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["wf_abi.cu", "wf_topk.cu", "wf_topk_tc.cu", "wf_attn.cu"]
+SOURCES = ["wf_abi.cu", "wf_topk.cu", "wf_topk_tc.cu", "wf_attn.cu", "wf_attn_bf16.cu", "wf_attn_f16.cu",
+           "wf_attn_f32.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -68,16 +69,23 @@ def build(verbose: bool = False, force: bool = False) -> Path:
     ]
     if verbose:
         common += ["-Xptxas", "-v"]
-    objs = []
+    # translation units compile concurrently (the attention instantiations dominate)
+    jobs = []
     for src in _sources():
         obj = obj_dir / (src.stem + ".o")
         cmd = [nvcc, *common, "-c", str(src), "-o", str(obj)]
-        res = subprocess.run(cmd, capture_output=True, text=True)
-        if res.returncode != 0:
-            raise RuntimeError(f"nvcc failed on {src.name}:\n{res.stderr}")
-        if verbose and res.stderr:
-            sys.stderr.write(res.stderr)
+        jobs.append((src, obj, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
+    objs = []
+    errors = []
+    for src, obj, proc in jobs:
+        _, err = proc.communicate()
+        if proc.returncode != 0:
+            errors.append(f"nvcc failed on {src.name}:\n{err}")
+        elif verbose and err:
+            sys.stderr.write(err)
         objs.append(str(obj))
+    if errors:
+        raise RuntimeError("\n".join(errors))
     tmp = LIB_PATH.with_suffix(".so.tmp")
     cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *objs, "-cudart", "static"]
     res = subprocess.run(cmd, capture_output=True, text=True)
