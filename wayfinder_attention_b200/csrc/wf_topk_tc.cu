@@ -83,7 +83,7 @@ struct TcParams {
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-constexpr int kXRounds = 11;  // pair exchanges for the bound: extrema + 10 bisection steps
+constexpr int kXRounds = 8;  // pair exchanges for the bound: extrema + 7 bisection steps
 
 template <int R, int EPL>
 struct Layout {
@@ -101,7 +101,8 @@ struct Layout {
   static constexpr size_t off_cnt = align_up(off_misc + 16, 16);   // per-row workspace slot counters
   static constexpr size_t off_thr = off_cnt + 4 * kM;     // per-row thresholds after a compaction
   static constexpr size_t off_xslot = off_thr + 4 * kM;  // [2 parities][kM rows][4] bisection exchange
-  static constexpr size_t off_queue = off_xslot + 4 * 2 * kM * 4;
+  static constexpr size_t off_xpair = off_xslot + 4 * 2 * kM * 4;  // [2 parities][2 warps][kM][4] pair sums
+  static constexpr size_t off_queue = off_xpair + 4 * 2 * 2 * kM * 4;
   static constexpr size_t off_merge = off_queue + 4 * (size_t)kQcap * kEpiWarps;  // per warp: K keys + K indices
   static constexpr size_t bytes = off_merge + (size_t)kEpiWarps * 128 * (4 + 4);
   // Slack to align the dynamic base to 1024, and at least 116 KB in total: two of
@@ -184,6 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* queues = reinterpret_cast<uint32_t*>(base + L::off_queue);
   int* cnt_s = reinterpret_cast<int*>(base + L::off_cnt);
   uint32_t* xslot = reinterpret_cast<uint32_t*>(base + L::off_xslot);
+  uint32_t* xpair = reinterpret_cast<uint32_t*>(base + L::off_xpair);
   float* thr_s = reinterpret_cast<float*>(base + L::off_thr);
   uint32_t* mkey = reinterpret_cast<uint32_t*>(base + L::off_merge);       // [warp][128]
   int* midx = reinterpret_cast<int*>(mkey + kEpiWarps * 128);              // [warp][128]
@@ -380,41 +382,60 @@ __global__ void __launch_bounds__(kThreads, 1)
     // same row through DSMEM (remote store + remote mbarrier arrive), and applies
     // the same decision, so both end with the same bound.  The K-th largest of the
     // union is the score of K distinct keys, so it lower-bounds the row's K-th score.
-    const uint32_t gbase = tmem_base + lane_base + 256;
+    // The two warps of a quadrant split each count (warp hf reads the column half
+    // hf of the row's maxima) and add their halves through shared memory first.
+    const uint32_t gbase = tmem_base + lane_base + 256 + (uint32_t)(hf * (kGroups / 2));
     int nf = 0;
     float mn = INFINITY, mx = -INFINITY;
 #pragma unroll 1
-    for (int blk = 0; blk < kGroups / 32; ++blk) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(gbase + blk * 32, v);
+    for (int blk = 0; blk < kGroups / 64; blk += 2) {
+      uint32_t v[2][32];
+      tmem_ld_32x32b_x32(gbase + blk * 32, v[0]);
+      tmem_ld_32x32b_x32(gbase + blk * 32 + 32, v[1]);
       tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float x = __uint_as_float(v[j]);
-        if (x > -INFINITY) {
-          ++nf;
-          mn = fminf(mn, x);
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float x = __uint_as_float(v[i][j]);
+          nf += x > -INFINITY ? 1 : 0;
+          mn = fminf(mn, x > -INFINITY ? x : INFINITY);
           mx = fmaxf(mx, x);
         }
-      }
     }
-    // one exchange round: send (a, b, c) to the peer thread of this row, receive its triple
-    auto swap3 = [&](int round, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t (&got)[3]) {
+    // add the pair's halves: [round parity][hf][row][3]; two parities because the
+    // partner may still read step i-1 while this warp writes step i+1
+    auto pair_sum3 = [&](int round, uint32_t (&x)[3]) {
+      uint32_t* mine = xpair + (((round & 1) * 2 + hf) * kM + r) * 4;
+      const uint32_t* other = xpair + (((round & 1) * 2 + (hf ^ 1)) * kM + r) * 4;
+      mine[0] = x[0];
+      mine[1] = x[1];
+      mine[2] = x[2];
+      pair_sync(pair_bar);
+      x[0] += other[0];
+      x[1] = __float_as_uint(fminf(__uint_as_float(x[1]), __uint_as_float(other[1])));
+      x[2] = __float_as_uint(fmaxf(__uint_as_float(x[2]), __uint_as_float(other[2])));
+    };
+    // one exchange with the peer CTA: send (a, b, c) to the peer's thread of this row
+    // (both warps of the quadrant send the same triple), receive the peer's triple
+    auto swap3 = [&](int round, const uint32_t (&x)[3], uint32_t (&got)[3]) {
       uint32_t* slot = xslot + ((round & 1) * kM + r) * 4;
       const uint32_t peer_slot = map_peer(slot, peer);
-      st_peer_u32(peer_slot, a0);
-      st_peer_u32(peer_slot + 4, a1);
-      st_peer_u32(peer_slot + 8, a2);
+      st_peer_u32(peer_slot, x[0]);
+      st_peer_u32(peer_slot + 4, x[1]);
+      st_peer_u32(peer_slot + 8, x[2]);
       mbar_arrive_peer(map_peer(&xbar[round], peer));
       if (!warp_wait_cluster(&xbar[round], 0)) { ok = false; why |= 256; }
       got[0] = slot[0];
       got[1] = slot[1];
       got[2] = slot[2];
     };
-    uint32_t got[3];
-    swap3(0, (uint32_t)nf, __float_as_uint(mn), __float_as_uint(mx), got);
-    const int nf_t = nf + (int)got[0];
-    float lo = fminf(mn, __uint_as_float(got[1])), hi = fmaxf(mx, __uint_as_float(got[2]));
+    uint32_t mine3[3] = {(uint32_t)nf, __float_as_uint(mn), __float_as_uint(mx)}, got[3];
+    pair_sum3(0, mine3);
+    swap3(0, mine3, got);
+    const int nf_t = (int)(mine3[0] + got[0]);
+    float lo = fminf(__uint_as_float(mine3[1]), __uint_as_float(got[1]));
+    float hi = fmaxf(__uint_as_float(mine3[2]), __uint_as_float(got[2]));
     const bool bis = nf_t >= p.K;
     if (!bis) lo = hi = 0.f;
     // every thread runs every step (tcgen05.ld is warp-collective and every step is
@@ -424,15 +445,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float mid = lo + 0.5f * (hi - lo);
       int c = 0;
 #pragma unroll 1
-      for (int blk = 0; blk < kGroups / 32; ++blk) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(gbase + blk * 32, v);
+      for (int blk = 0; blk < kGroups / 64; blk += 2) {
+        uint32_t v[2][32];
+        tmem_ld_32x32b_x32(gbase + blk * 32, v[0]);
+        tmem_ld_32x32b_x32(gbase + blk * 32 + 32, v[1]);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) c += __uint_as_float(v[j]) >= mid ? 1 : 0;
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) c += __uint_as_float(v[i][j]) >= mid ? 1 : 0;
       }
-      swap3(1 + it, (uint32_t)c, 0u, 0u, got);
-      if (c + (int)got[0] >= p.K) lo = mid;
+      uint32_t x3[3] = {(uint32_t)c, 0u, 0u};
+      pair_sum3(1 + it, x3);
+      swap3(1 + it, x3, got);
+      if ((int)(x3[0] + got[0]) >= p.K) lo = mid;
       else hi = mid;
     }
     const float theta = bis ? lo : -INFINITY;
