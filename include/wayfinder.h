@@ -11,6 +11,7 @@
  *   wf_causal_topk            <- routing_attention/kernels/causal_topk.py:470-521   causal_topk()
  *   wf_sparse_attention       <- routing_attention/kernels/fused_sparse.py:275-324  sparse_meat_attention()
  *   wf_fused_sparse_attention <- routing_attention/kernels/fused_sparse.py:327-356  fused_sparse_attention()
+ *   wf_fused_sparse_attention_host: the same operator on host-resident tensors (copies overlapped)
  */
 #ifndef WAYFINDER_H_
 #define WAYFINDER_H_
@@ -170,6 +171,42 @@ WF_API int wf_fused_sparse_attention(const void* q_addr, const void* k_addr, int
                               int32_t row_start, int32_t* idx_out, void* out, int32_t out_dtype,
                               const int64_t* out_strides, void* workspace, size_t workspace_bytes,
                               int32_t* status, void* stream);
+
+/*
+ * wf_fused_sparse_attention for HOST-resident inputs and outputs, with the copies
+ * overlapped with the kernels.  No counterpart in the reference (whose operator
+ * takes device tensors); it serves callers whose activations live in pinned host
+ * memory.  Schedule (three caller streams):
+ *   h2d_stream : q_addr, k_addr | q,k,v rows of chunk 0 | ... | chunk chunks-1
+ *   stream     : retrieval of all rows | attention of chunk 0 | ... (each chunk
+ *                waits for its rows; attention of rows [a, e) reads K/V rows < e only)
+ *   d2h_stream : idx | out rows of chunk 0 | ...
+ * On return everything is enqueued and `stream` waits for the last download, so
+ * the host outputs are valid once `stream` has completed.  Results are identical
+ * to wf_fused_sparse_attention on the same data.
+ *
+ *   q_addr_h, k_addr_h : (B, T, R) host addresses, contiguous
+ *   q_h, k_h, v_h      : (B, H, T, D) host tensors with element strides q/k/v_strides,
+ *                        stride(D) = 1 and either (B,T,H,D)-major rows (stride(T) = H*D,
+ *                        stride(H) = D) or head-major rows (stride(T) = D)
+ *   idx_h              : (B, T, K_eff) int32 host output, contiguous
+ *   out_h              : (B, H, T, D) host output with out_strides (same layout rule)
+ *   d_*                : device staging buffers of the same shapes and strides as the host
+ *                        tensors (addresses and idx contiguous), reused across calls
+ *   workspace          : device scratch of wf_causal_topk_workspace_bytes(B, T, T, R, top_k, addr_dtype)
+ *   chunks             : number of query-row chunks (1 .. min(64, T)); 4-8 suits T >= 4096
+ * top_k must be >= 1 (K_eff = min(top_k, T)).  Host buffers that are not page-locked
+ * still work, with copies that no longer overlap.
+ */
+WF_API int wf_fused_sparse_attention_host(const void* q_addr_h, const void* k_addr_h, int32_t addr_dtype, int32_t R,
+                                          const void* q_h, const void* k_h, const void* v_h, int32_t dtype,
+                                          int64_t B, int64_t H, int64_t T, int32_t D, const int64_t* q_strides,
+                                          const int64_t* k_strides, const int64_t* v_strides, int32_t top_k,
+                                          float scale, int32_t pad_mode, int32_t chunks, int32_t* idx_h,
+                                          void* out_h, int32_t out_dtype, const int64_t* out_strides,
+                                          void* d_q_addr, void* d_k_addr, void* d_q, void* d_k, void* d_v,
+                                          int32_t* d_idx, void* d_out, void* workspace, size_t workspace_bytes,
+                                          int32_t* status, void* stream, void* h2d_stream, void* d2h_stream);
 
 #ifdef __cplusplus
 }

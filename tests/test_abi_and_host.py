@@ -68,6 +68,24 @@ def test_invalid_arguments_fail_without_gpu():
     assert rc == _lib.WF_ERR_UNSUPPORTED and b"maximum" in lib.wf_last_error()
 
 
+def test_host_pipeline_entry_validates_before_enqueueing():
+    lib = _lib.load_library()
+    p = ctypes.c_void_p(4096)
+    B, H, T, D, R = 1, 2, 256, 64, 32
+    rows = _i64(T * H * D, D, H * D, 1)  # (B,T,H,D)-major
+    bad = _i64(T * H * D, 1, H * D, 2)   # stride(D) != 1
+
+    def call(top_k=16, chunks=4, qs=rows):
+        return lib.wf_fused_sparse_attention_host(p, p, 0, R, p, p, p, 0, B, H, T, D, qs, rows, rows, top_k, 1.0, 0,
+                                                  chunks, p, p, 0, rows, p, p, p, p, p, p, p, None, 0, None, None,
+                                                  None, None)
+
+    assert call(top_k=0) == _lib.WF_ERR_INVALID_ARGUMENT and b"top_k" in lib.wf_last_error()
+    assert call(chunks=0) == _lib.WF_ERR_INVALID_ARGUMENT and b"chunks" in lib.wf_last_error()
+    assert call(chunks=65) == _lib.WF_ERR_INVALID_ARGUMENT
+    assert call(qs=bad) == _lib.WF_ERR_UNSUPPORTED and b"stride" in lib.wf_last_error()
+
+
 def test_python_api_validates_like_reference():
     a = torch.zeros(1, 8, 32)
     with pytest.raises(ValueError, match="shape mismatch"):

@@ -3,7 +3,8 @@
 Public API (names and arguments of the reference's ``routing_attention``):
   causal_topk, fused_sparse_attention, sparse_meat_attention, SparseMeatConfig,
   LearnedAddressSparseAttention, LearnedAddressModule, RetrievalConfig,
-  TransformerLM (the decoder harness).
+  TransformerLM (the decoder harness); HostFusedSparseAttention runs the fused
+  op on pinned host tensors with upload, compute and download overlapped.
 
 The compute runs in ``libwayfinder_sm100.so`` (C ABI: ``include/wayfinder.h``);
 there is no CPU path.
@@ -19,6 +20,7 @@ from .attention import (
 )
 from .causal_topk import causal_topk, causal_topk_available, promote_compute_dtype
 from .decoder import DenseSDPAAttention, TransformerBlock, TransformerLM
+from .host_pipeline import HostFusedSparseAttention, host_fused_sparse_attention
 from .fused_sparse import (
     SparseMeatConfig,
     fused_sparse_attention,
@@ -34,6 +36,8 @@ __all__ = [
     "fused_sparse_attention",
     "fused_sparse_attention_available",
     "sparse_meat_attention",
+    "HostFusedSparseAttention",
+    "host_fused_sparse_attention",
     "SparseMeatConfig",
     "LearnedAddressModule",
     "LearnedAddressSparseAttention",

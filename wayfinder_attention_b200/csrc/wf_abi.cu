@@ -285,4 +285,147 @@ int wf_causal_topk_noalloc(const void* q_addr, const void* k_addr, int32_t dtype
                         row_stride, row_start, idx_out, scratch, need, status, stream);
 }
 
+
+namespace {
+// Row-chunk copy plan of a (B, H, T, D) tensor: rows [a, e) of every (b[, h]) as
+// 2D copies.  kind 1: (B,T,H,D)-major rows, kind 2: head-major rows.
+int row_layout(const int64_t* s, int64_t H, int32_t D) {
+  if (s[3] != 1) return 0;
+  if (s[1] == D && s[2] == H * D) return 1;
+  if (s[2] == D) return 2;
+  return 0;
+}
+
+cudaError_t copy_rows(char* dst, const char* src, int esz, int kind, int64_t B, int64_t H, int32_t D,
+                      const int64_t* s, int64_t a, int64_t e, cudaMemcpyKind dir, cudaStream_t st) {
+  if (kind == 1) {
+    const size_t width = (size_t)(e - a) * H * D * esz, off = (size_t)(a * s[2]) * esz;
+    if (B == 1) return cudaMemcpyAsync(dst + off, src + off, width, dir, st);
+    const size_t pitch = (size_t)s[0] * esz;
+    return cudaMemcpy2DAsync(dst + off, pitch, src + off, pitch, width, (size_t)B, dir, st);
+  }
+  const size_t width = (size_t)(e - a) * D * esz, off = (size_t)(a * D) * esz, pitch = (size_t)s[1] * esz;
+  if (s[0] == H * s[1]) return cudaMemcpy2DAsync(dst + off, pitch, src + off, pitch, width, (size_t)(B * H), dir, st);
+  for (int64_t b = 0; b < B; ++b) {
+    const size_t ob = off + (size_t)(b * s[0]) * esz;
+    cudaError_t rc = cudaMemcpy2DAsync(dst + ob, pitch, src + ob, pitch, width, (size_t)H, dir, st);
+    if (rc != cudaSuccess) return rc;
+  }
+  return cudaSuccess;
+}
+
+// Events of one host-pipelined call; destroyed once recorded (the runtime frees
+// them after they complete).
+struct EventSet {
+  cudaEvent_t ev[256];
+  int n = 0;
+  cudaEvent_t make() {
+    cudaEvent_t e = nullptr;
+    if (n < 256 && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess) ev[n++] = e;
+    return e;
+  }
+  ~EventSet() {
+    for (int i = 0; i < n; ++i) cudaEventDestroy(ev[i]);
+  }
+};
+}  // namespace
+
+int wf_fused_sparse_attention_host(const void* q_addr_h, const void* k_addr_h, int32_t addr_dtype, int32_t R,
+                                   const void* q_h, const void* k_h, const void* v_h, int32_t dtype, int64_t B,
+                                   int64_t H, int64_t T, int32_t D, const int64_t* q_strides,
+                                   const int64_t* k_strides, const int64_t* v_strides, int32_t top_k, float scale,
+                                   int32_t pad_mode, int32_t chunks, int32_t* idx_h, void* out_h,
+                                   int32_t out_dtype, const int64_t* out_strides, void* d_q_addr, void* d_k_addr,
+                                   void* d_q, void* d_k, void* d_v, int32_t* d_idx, void* d_out, void* workspace,
+                                   size_t workspace_bytes, int32_t* status, void* stream, void* h2d_stream,
+                                   void* d2h_stream) {
+  if (top_k < 1) return fail(WF_ERR_INVALID_ARGUMENT, "wf_fused_sparse_attention_host: top_k must be >= 1, got %d", top_k);
+  if (!q_addr_h || !k_addr_h || !q_h || !k_h || !v_h || !idx_h || !out_h || !d_q_addr || !d_k_addr || !d_q ||
+      !d_k || !d_v || !d_idx || !d_out || !q_strides || !k_strides || !v_strides || !out_strides)
+    return fail(WF_ERR_INVALID_ARGUMENT, "wf_fused_sparse_attention_host: null pointer argument");
+  if (B < 1 || H < 1 || T < 1) return fail(WF_ERR_INVALID_ARGUMENT, "wf_fused_sparse_attention_host: empty problem");
+  if (chunks < 1 || chunks > 64 || chunks > T)
+    return fail(WF_ERR_INVALID_ARGUMENT, "chunks must be in [1, min(64, T)], got %d", chunks);
+  if (!valid_dtype(dtype) || !valid_dtype(out_dtype) || !valid_dtype(addr_dtype))
+    return fail(WF_ERR_INVALID_ARGUMENT, "unknown dtype");
+  const int kq = row_layout(q_strides, H, D), kk = row_layout(k_strides, H, D), kv = row_layout(v_strides, H, D),
+            ko = row_layout(out_strides, H, D);
+  if (!kq || !kk || !kv || !ko)
+    return fail(WF_ERR_UNSUPPORTED, "host q/k/v/out need unit stride(D) and (B,T,H,D)-major or head-major rows");
+  const int32_t k_eff = (int32_t)(top_k < T ? top_k : T);
+  const int64_t as[3] = {T * R, (int64_t)R, 1};
+  const int64_t is[3] = {T * (int64_t)k_eff, (int64_t)k_eff, 1};
+  // full validation of both launches before anything is enqueued
+  {
+    int32_t rt = 0, rs = 1, r0 = 0, ke = 0;
+    int rc = check_topk(d_q_addr, d_k_addr, addr_dtype, B, T, T, R, as, as, top_k, pad_mode, rt, rs, r0, d_idx, &ke);
+    if (rc) return rc;
+    rc = check_attn(d_q, d_k, d_v, dtype, d_idx, B, H, T, T, D, k_eff, q_strides, k_strides, v_strides, is, scale,
+                    pad_mode == WF_PAD_MASKED ? WF_ATTN_MASK_NEGATIVE : 0, d_out, out_dtype, out_strides);
+    if (rc) return rc;
+  }
+  cudaStream_t sm = static_cast<cudaStream_t>(stream), si = static_cast<cudaStream_t>(h2d_stream),
+               so = static_cast<cudaStream_t>(d2h_stream);
+  const int esz = dtype_size(dtype), osz = dtype_size(out_dtype), asz = dtype_size(addr_dtype);
+  EventSet evs;
+  cudaError_t ce = cudaSuccess;
+#define WF_CK(x)                                                            \
+  do {                                                                      \
+    ce = (x);                                                               \
+    if (ce != cudaSuccess) return cuda_fail((int)ce, "wf_fused_sparse_attention_host"); \
+  } while (0)
+#define WF_EV(name)                                                                             \
+  cudaEvent_t name = evs.make();                                                                \
+  if (!name) return fail(WF_ERR_CUDA, "wf_fused_sparse_attention_host: event creation failed")
+  // the copy streams start after the work already queued on `stream` (the previous
+  // call's kernels may still read the staging buffers)
+  WF_EV(e_start);
+  WF_CK(cudaEventRecord(e_start, sm));
+  WF_CK(cudaStreamWaitEvent(si, e_start, 0));
+  WF_CK(cudaStreamWaitEvent(so, e_start, 0));
+  const size_t abytes = (size_t)(B * T * R) * asz;
+  WF_CK(cudaMemcpyAsync(d_q_addr, q_addr_h, abytes, cudaMemcpyHostToDevice, si));
+  WF_CK(cudaMemcpyAsync(d_k_addr, k_addr_h, abytes, cudaMemcpyHostToDevice, si));
+  WF_EV(e_addr);
+  WF_CK(cudaEventRecord(e_addr, si));
+  cudaEvent_t e_rows[64];
+  for (int c = 0; c < chunks; ++c) {
+    const int64_t a = T * c / chunks, e = T * (c + 1) / chunks;
+    WF_CK(copy_rows((char*)d_q, (const char*)q_h, esz, kq, B, H, D, q_strides, a, e, cudaMemcpyHostToDevice, si));
+    WF_CK(copy_rows((char*)d_k, (const char*)k_h, esz, kk, B, H, D, k_strides, a, e, cudaMemcpyHostToDevice, si));
+    WF_CK(copy_rows((char*)d_v, (const char*)v_h, esz, kv, B, H, D, v_strides, a, e, cudaMemcpyHostToDevice, si));
+    WF_EV(er);
+    WF_CK(cudaEventRecord(er, si));
+    e_rows[c] = er;
+  }
+  WF_CK(cudaStreamWaitEvent(sm, e_addr, 0));
+  int rc = wf_causal_topk(d_q_addr, d_k_addr, addr_dtype, B, T, T, R, as, as, top_k, pad_mode, 0, 1, 0, d_idx,
+                          workspace, workspace_bytes, status, stream);
+  if (rc) return rc;
+  WF_EV(e_idx);
+  WF_CK(cudaEventRecord(e_idx, sm));
+  WF_CK(cudaStreamWaitEvent(so, e_idx, 0));
+  WF_CK(cudaMemcpyAsync(idx_h, d_idx, (size_t)(B * T) * k_eff * sizeof(int32_t), cudaMemcpyDeviceToHost, so));
+  for (int c = 0; c < chunks; ++c) {
+    const int64_t a = T * c / chunks, e = T * (c + 1) / chunks;
+    WF_CK(cudaStreamWaitEvent(sm, e_rows[c], 0));
+    rc = wf_sparse_attention(static_cast<const char*>(d_q) + (size_t)(a * q_strides[2]) * esz, d_k, d_v, dtype,
+                             d_idx + a * k_eff, B, H, e - a, T, D, k_eff, q_strides, k_strides, v_strides, is, scale,
+                             pad_mode == WF_PAD_MASKED ? WF_ATTN_MASK_NEGATIVE : 0,
+                             static_cast<char*>(d_out) + (size_t)(a * out_strides[2]) * osz, out_dtype, out_strides,
+                             status, stream);
+    if (rc) return rc;
+    WF_EV(ed);
+    WF_CK(cudaEventRecord(ed, sm));
+    WF_CK(cudaStreamWaitEvent(so, ed, 0));
+    WF_CK(copy_rows((char*)out_h, (const char*)d_out, osz, ko, B, H, D, out_strides, a, e, cudaMemcpyDeviceToHost, so));
+  }
+  WF_EV(e_fin);
+  WF_CK(cudaEventRecord(e_fin, so));
+  WF_CK(cudaStreamWaitEvent(sm, e_fin, 0));
+#undef WF_CK
+#undef WF_EV
+  return ok();
+}
+
 }  // extern "C"

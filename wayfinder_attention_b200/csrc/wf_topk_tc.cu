@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int key_end = min(g0 + nrows, p.Tk);
   const int nchunks = (key_end + kN - 1) / kN;
   const int n_own = nchunks > (int)rank ? (nchunks - (int)rank + 1) / 2 : 0;
-  const int n_work = 2 * n_own;
+  const int n_work = (WF_TOPK_SKIP & 2) ? n_own : 2 * n_own;  // pass 1 + pass 2 items
 
   if (warp == kEpiWarps && lane == 0) {
     for (int s = 0; s < S; ++s) {
@@ -531,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // The vote reads the counter before the partner's last reservation may be
         // visible (up to 32 more), hence the 96 margin; after the barrier the
         // counts are exact and rows within 64 of the end are compacted.
-        if (pair_any(pair_bar, row_ok && cnt_s[r] + 96 > kWcap)) {
+        if (!((WF_TOPK_SKIP & 1) && i == 1) && pair_any(pair_bar, row_ok && cnt_s[r] + 96 > kWcap)) {
           flush(stage, c);
           pair_sync(pair_bar);
           if (hf == 0) {
@@ -682,8 +682,10 @@ __global__ void __launch_bounds__(kFinWarps * 32, 2) topk_finalize_kernel(const 
   const int64_t row = (int64_t)blockIdx.x * kFinWarps + warp;
   if (row >= (int64_t)p.B * p.Tq) return;
   const int n1 = p.ws_cnt[row * 2], n2 = p.ws_cnt[row * 2 + 1];
-  // typical rows hold about 2.6 K candidates; the wide form covers full workspace slices
-  if (n1 + n2 <= 12 * 32) finalize_row<12, SE>(p, row, n1, n2, lane, skey[warp], sidx[warp]);
+  // with the pair's shared bound a row typically holds 1.1-1.5 K candidates (K <= 128);
+  // the wider forms cover larger K and full workspace slices
+  if (n1 + n2 <= 6 * 32) finalize_row<6, SE>(p, row, n1, n2, lane, skey[warp], sidx[warp]);
+  else if (n1 + n2 <= 12 * 32) finalize_row<12, SE>(p, row, n1, n2, lane, skey[warp], sidx[warp]);
   else finalize_row<2 * kWcap / 32, SE>(p, row, n1, n2, lane, skey[warp], sidx[warp]);
 }
 

@@ -65,6 +65,7 @@ def _launch_attention(
     mask_negative: bool,
     out_dtype: torch.dtype | None,
     status: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     dev = _lib.require_cuda(q, k, v, indices)
     lib = _lib.load_library()
@@ -73,7 +74,10 @@ def _launch_attention(
     K = indices.shape[-1]
     if indices.dim() != 3 or indices.shape[0] != B or indices.shape[1] != Tq:
         raise ValueError(f"indices must have shape {(B, Tq, K)}, got {tuple(indices.shape)}")
-    out = torch.empty(B, H, Tq, D, dtype=out_dtype or q.dtype, device=dev)
+    if out is None:
+        out = torch.empty(B, H, Tq, D, dtype=out_dtype or q.dtype, device=dev)
+    elif tuple(out.shape) != (B, H, Tq, D) or out.device != dev or (out_dtype and out.dtype != out_dtype):
+        raise ValueError(f"out must be a {(B, H, Tq, D)} tensor on {dev}")
     if K == 0:
         # softmax over an empty set: the reference's sum over zero rows is 0
         return out.zero_()
