@@ -100,7 +100,7 @@ WF_API size_t wf_causal_topk_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, 
  * Allocation-free variant of wf_causal_topk.  It has no counterpart in the
  * reference.  It is for callers that cannot allocate device memory at all (an
  * allocator-less runtime, or code running where cudaMalloc is not permitted): the
- * retrieval scratch comes from a fixed 8 MiB device array built into this library,
+ * retrieval scratch comes from a fixed 16 MiB device array built into this library,
  * which every GPU that loads the library keeps reserved until the process exits.
  * Same arguments and results as wf_causal_topk without the workspace; B*Tq is
  * limited to what fits in that array (2044 query rows for K <= 128; larger requests

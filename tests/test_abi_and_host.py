@@ -151,7 +151,7 @@ def test_synthetic_inputs_are_seeded_and_laid_out_like_the_module():
 
 def test_workspace_query():
     lib = _lib.load_library()
-    assert lib.wf_causal_topk_workspace_bytes(1, 16384, 16384, 32, 128, _lib.WF_DTYPE_BF16) == 16384 * (2 * 256 * 8 + 8)
-    assert lib.wf_causal_topk_workspace_bytes(2, 100, 100, 32, 64, _lib.WF_DTYPE_F16) == 200 * (2 * 256 * 8 + 8)
+    assert lib.wf_causal_topk_workspace_bytes(1, 16384, 16384, 32, 128, _lib.WF_DTYPE_BF16) == 16384 * (4 * 256 * 8 + 16)
+    assert lib.wf_causal_topk_workspace_bytes(2, 100, 100, 32, 64, _lib.WF_DTYPE_F16) == 200 * (4 * 256 * 8 + 16)
     assert lib.wf_causal_topk_workspace_bytes(1, 2048, 2048, 32, 128, _lib.WF_DTYPE_F32) == 0  # CUDA-core path
     assert lib.wf_causal_topk_workspace_bytes(1, 2048, 2048, 32, 256, _lib.WF_DTYPE_BF16) == 0

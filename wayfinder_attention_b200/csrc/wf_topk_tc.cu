@@ -58,8 +58,9 @@ constexpr int kN = 128;   // keys per chunk = MMA N
 constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant
 constexpr int kThreads = (kEpiWarps + 1) * 32;
 constexpr int kGroups = 256;  // pass-1 key groups per row (TMEM columns 256..511)
-constexpr int kQcap = 1024;   // rescoring queue entries per warp
-constexpr int kWcap = 256;    // workspace candidates per (row, CTA); a full row is compacted to its top-K
+constexpr int kQcap = 2048;   // rescoring queue entries per warp (one chunk admits at most 64 x 32)
+constexpr int kWcap = 256;    // workspace candidates per (row, CTA, warp); a full list is compacted to its top-K
+constexpr int kLists = 4;     // candidate lists per row: 2 CTAs x 2 selection warps
 constexpr unsigned kFullMask = 0xffffffffu;
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr float kEpsScale = 1.0f / 8192.0f;
@@ -67,6 +68,18 @@ constexpr int kMaxDevices = 64;
 constexpr size_t kMaxSmem = 232448;
 #ifndef WF_TOPK_SKIP
 #define WF_TOPK_SKIP 0  // profiling builds only: bit mask of phases to skip
+#endif
+
+#ifndef WF_TOPK_PROF
+#define WF_TOPK_PROF 0  // profiling builds only: per-phase SM-cycle counters of the selection warps
+#endif
+#if WF_TOPK_PROF
+__device__ unsigned long long g_topk_prof[16];
+#define PROF_T(v) const long long v = clock64()
+#define PROF_ADD(slot, d) prof_acc[slot] += (unsigned long long)(d)
+#else
+#define PROF_T(v)
+#define PROF_ADD(slot, d)
 #endif
 
 struct TcParams {
@@ -77,8 +90,8 @@ struct TcParams {
   int rt, rs, r0;
   int32_t* idx;
   int32_t* status;
-  uint64_t* ws;      // [B*Tq][2][kWcap] candidate composites (key << 32 | ~index)
-  int32_t* ws_cnt;   // [B*Tq][2] candidate counts
+  uint64_t* ws;      // [B*Tq][kLists][kWcap] candidate composites (key << 32 | ~index)
+  int32_t* ws_cnt;   // [B*Tq][kLists] candidate counts
 };
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -98,9 +111,7 @@ struct Layout {
   static constexpr size_t off_bar = align_up(off_kmax + sizeof(float) * S, 8);
   static constexpr size_t n_bar = 3 * S + 2 + kXRounds;  // full, mdone, done, qbar, kbar, xbar[rounds]
   static constexpr size_t off_misc = off_bar + 8 * n_bar;  // tmem base, kmax own, kmax peer, abort
-  static constexpr size_t off_cnt = align_up(off_misc + 16, 16);   // per-row workspace slot counters
-  static constexpr size_t off_thr = off_cnt + 4 * kM;     // per-row thresholds after a compaction
-  static constexpr size_t off_xslot = off_thr + 4 * kM;  // [2 parities][kM rows][4] bisection exchange
+  static constexpr size_t off_xslot = align_up(off_misc + 16, 16);  // [2 parities][kM rows][4] bisection exchange
   static constexpr size_t off_xpair = off_xslot + 4 * 2 * kM * 4;  // [2 parities][2 warps][kM][4] pair sums
   static constexpr size_t off_queue = off_xpair + 4 * 2 * 2 * kM * 4;
   static constexpr size_t off_merge = off_queue + 4 * (size_t)kQcap * kEpiWarps;  // per warp: K keys + K indices
@@ -118,18 +129,9 @@ struct Layout {
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, kWaitLimitNs));
 }
-// Named barrier of the 64 threads of one quadrant's two warps, and its OR-reduction.
+// Named barrier of the 64 threads of one quadrant's two warps.
 __device__ __forceinline__ void pair_sync(int id) {
   asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
-}
-__device__ __forceinline__ bool pair_any(int id, bool v) {
-  uint32_t r;
-  asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, 64, p;\n\t"
-               "selp.u32 %0, 1, 0, q;\n\t}"
-               : "=r"(r)
-               : "r"((uint32_t)v), "r"(id)
-               : "memory");
-  return r != 0;
 }
 
 __device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity) {
@@ -183,10 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* kmax_own_s = tmem_base_s + 1;
   uint32_t* kmax_in_s = tmem_base_s + 2;
   uint32_t* queues = reinterpret_cast<uint32_t*>(base + L::off_queue);
-  int* cnt_s = reinterpret_cast<int*>(base + L::off_cnt);
   uint32_t* xslot = reinterpret_cast<uint32_t*>(base + L::off_xslot);
   uint32_t* xpair = reinterpret_cast<uint32_t*>(base + L::off_xpair);
-  float* thr_s = reinterpret_cast<float*>(base + L::off_thr);
   uint32_t* mkey = reinterpret_cast<uint32_t*>(base + L::off_merge);       // [warp][128]
   int* midx = reinterpret_cast<int*>(mkey + kEpiWarps * 128);              // [warp][128]
 
@@ -323,13 +323,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st_32x32b_x32(tmem_base + lane_base + 256 + par * kN + (2 * hf + i) * 32, ninf);
       tmem_st_wait();
     }
-    if (hf == 0) {
-      cnt_s[r] = 0;
-      thr_s[r] = -INFINITY;
-    }
     ok = warp_wait(qbar, 0);
     if (!ok) why |= 64;
 
+#if WF_TOPK_PROF
+    unsigned long long prof_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#endif
+    PROF_T(tp1s);
     // ---------------- pass 1: group maxima of tensor-core scores (this warp's slices)
     for (int w = 0; w < n_own && ok; ++w) {
       const int s = w % S;
@@ -370,12 +370,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&done[s]);
     }
-    // both warps' group maxima (and cnt_s / thr_s) are complete and visible to the pair
+    // both warps' group maxima are complete and visible to the pair
     tmem_st_wait();
     tc_fence_before();
     pair_sync(pair_bar);
     tc_fence_after();
 
+    PROF_T(tp1e);
+    PROF_ADD(0, tp1e - tp1s);
     // ---------------- lower bound on the K-th best score from the pair's 512 group maxima
     // Both CTAs bisect the same value range over the union of their maxima: each
     // step counts its own maxima >= mid, swaps the count with the peer thread of the
@@ -471,10 +473,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float eps = kEpsScale * qabs * kpair;
     float lim = theta > -INFINITY ? theta - eps : -INFINITY;
 
+    PROF_T(tbe);
+    PROF_ADD(1, tbe - tp1e);
     // ---------------- pass 2: admit, rescore exactly, keep candidates in the workspace
     uint32_t* queue = queues + warp * kQcap;
     const int64_t row0 = (int64_t)b * p.Tq + l0 + 32 * qd;  // first row of this quadrant
     int qsize = 0;  // warp-uniform
+
+    // This warp's candidates of row r go to its own list (CTA rank, column half hf):
+    // the count lives in the lane's register, so no slot is shared with another warp.
+    int cnt = 0;
 
     auto flush = [&](const unsigned char* stage, int c) {
       __syncwarp();
@@ -482,25 +490,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ent = queue[e];
         const int lr = ent & 31, jj = (ent >> 5) & 127, dest = (int)(ent >> 12);
         const float ex = dot_swizzled<TI, ROWB>(qs, 32 * qd + lr, stage, jj);
-        p.ws[((row0 + lr) * 2 + rank) * kWcap + dest] =
+        p.ws[(((row0 + lr) * 2 + rank) * 2 + hf) * kWcap + dest] =
             ((uint64_t)ordered_key(ex) << 32) | (uint32_t)(~(uint32_t)(c * kN + jj));
       }
       __syncwarp();
       qsize = 0;
     };
 
-    // Every warp runs the same number of rounds (2 per chunk) so the pair
-    // barriers inside stay matched even if a wait of this warp gives up.
     bool alive = ok;
     for (int w = n_own; w < n_work; ++w) {
       const int s = w % S;
       const uint32_t ph = (uint32_t)(w / S) & 1u;
+      PROF_T(tw0);
       if (alive && (!warp_wait(&mdone[s], ph) || !warp_wait(&full[s], ph))) {
         alive = false;
         ok = false;
         why |= 512;
       }
       tc_fence_after();
+      PROF_T(tw1);
+      PROF_ADD(2, tw1 - tw0);
       const int c = chunk_of(w);
       const unsigned char* stage = ks + s * L::STAGE_STRIDE;
       const uint32_t acc = tmem_base + lane_base + (uint32_t)((w & 1) * kN);
@@ -522,77 +531,80 @@ __global__ void __launch_bounds__(kThreads, 1)
           masks[i] = m;
         }
       }
-#pragma unroll 1
-      for (int i = 0; i < 2; ++i) {
-        const int sl = 2 * hf + i;
-        uint32_t m = masks[i];
-        const int np = __popc(m);
-        // A round adds at most 64 candidates to a row (32 per warp of the pair).
-        // The vote reads the counter before the partner's last reservation may be
-        // visible (up to 32 more), hence the 96 margin; after the barrier the
-        // counts are exact and rows within 64 of the end are compacted.
-        if (!((WF_TOPK_SKIP & 1) && i == 1) && pair_any(pair_bar, row_ok && cnt_s[r] + 96 > kWcap)) {
-          flush(stage, c);
-          pair_sync(pair_bar);
-          if (hf == 0) {
-            unsigned need = __ballot_sync(kFullMask, row_ok && cnt_s[r] + 64 > kWcap);
-            while (need) {
-              const int ln = __ffs(need) - 1;
-              need &= need - 1;
-              const int rr = 32 * qd + ln;
-              const int n = cnt_s[rr];
-              uint64_t* wrow = p.ws + ((row0 + ln) * 2 + rank) * kWcap;
-              uint32_t kk[kWcap / 32];
-              int ii[kWcap / 32];
+      PROF_T(tw2);
+      PROF_ADD(3, tw2 - tw1);
+      const int np = __popc(masks[0]) + __popc(masks[1]);
+      // A list that this chunk could overflow is compacted to its exact top-K first
+      // (queued entries written out beforehand); that also raises the row's threshold.
+      unsigned need = __ballot_sync(kFullMask, cnt + np > kWcap);
+      if (need) {
+        flush(stage, c);
+        uint32_t* bk = mkey + warp * 128;
+        int* bi = midx + warp * 128;
+        while (need) {
+          const int ln = __ffs(need) - 1;
+          need &= need - 1;
+          const int n = __shfl_sync(kFullMask, cnt, ln);
+          uint64_t* wrow = p.ws + (((row0 + ln) * 2 + rank) * 2 + hf) * kWcap;
+          uint32_t kk[kWcap / 32];
+          int ii[kWcap / 32];
 #pragma unroll
-              for (int t = 0; t < kWcap / 32; ++t) {
-                const int e = t * 32 + lane;
-                const uint64_t cv = e < n ? wrow[e] : 0ull;
-                kk[t] = (uint32_t)(cv >> 32);
-                ii[t] = e < n ? (int)(~(uint32_t)cv) : INT_MAX;
-              }
-              uint32_t* bk = mkey + qd * 128;
-              int* bi = midx + qd * 128;
-              const uint32_t tau = select_compact<kWcap / 32>(kk, ii, n, p.K, lane, bk, bi);
-              for (int e = lane; e < p.K; e += 32) wrow[e] = ((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e]);
-              __syncwarp();
-              if (lane == 0) {
-                cnt_s[rr] = p.K;
-                thr_s[rr] = key_to_float(tau);
-              }
-              __syncwarp();
-            }
+          for (int t = 0; t < kWcap / 32; ++t) {
+            const int e = t * 32 + lane;
+            const uint64_t cv = e < n ? wrow[e] : 0ull;
+            kk[t] = (uint32_t)(cv >> 32);
+            ii[t] = e < n ? (int)(~(uint32_t)cv) : INT_MAX;
           }
-          pair_sync(pair_bar);
-          lim = fmaxf(lim, thr_s[r] - eps);
+          const uint32_t tau = select_compact<kWcap / 32>(kk, ii, n, p.K, lane, bk, bi);
+          for (int e = lane; e < p.K; e += 32) wrow[e] = ((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e]);
+          __syncwarp();
+          if (lane == ln) {
+            cnt = p.K;
+            lim = fmaxf(lim, key_to_float(tau) - eps);
+          }
         }
-        // reserve workspace slots for this warp's admitted keys of the row
-        const int base = np ? atomicAdd(&cnt_s[r], np) : 0;
-        int incl = np;
+      }
+      // slots of this lane's admitted keys: its own list, no other writer
+      const int base = cnt;
+      cnt += np;
+      int incl = np;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int t = __shfl_up_sync(kFullMask, incl, o);
-          if (lane >= o) incl += t;
-        }
-        const int total = __shfl_sync(kFullMask, incl, 31);
-        if (qsize + total > kQcap) flush(stage, c);
-        int pos = qsize + incl - np;
-        int k = 0;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(kFullMask, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const int total = __shfl_sync(kFullMask, incl, 31);
+      if (qsize + total > kQcap) flush(stage, c);
+      uint32_t* qp = queue + qsize + incl - np;
+      uint32_t slot = (uint32_t)base;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        uint32_t m = masks[i];
         while (m) {
           const int j = __ffs(m) - 1;
           m &= m - 1;
-          queue[pos + k] = (uint32_t)lane | ((uint32_t)(sl * 32 + j) << 5) | ((uint32_t)(base + k) << 12);
-          ++k;
+          *qp++ = (uint32_t)lane | ((uint32_t)((2 * hf + i) * 32 + j) << 5) | (slot++ << 12);
         }
-        qsize += total;
       }
+      qsize += total;
+      PROF_T(tw3);
+      PROF_ADD(4, tw3 - tw2);
       flush(stage, c);  // the stage is about to be released
+      PROF_T(tw4);
+      PROF_ADD(5, tw4 - tw3);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&done[s]);
     }
-    pair_sync(pair_bar);
-    if (hf == 0 && row_ok) p.ws_cnt[(row0 + lane) * 2 + rank] = cnt_s[r];
+    if (row_ok) p.ws_cnt[((row0 + lane) * 2 + rank) * 2 + hf] = cnt;
+#if WF_TOPK_PROF
+    PROF_T(tend);
+    PROF_ADD(6, tend - tbe);
+    PROF_ADD(7, tend - tp1s);
+    if (lane == 0)
+      for (int i = 0; i < 8; ++i) atomicAdd(&g_topk_prof[i], prof_acc[i]);
+    if (lane == 0) atomicAdd(&g_topk_prof[8], 1ull);
+#endif
   }
   if (!ok && p.status) atomicOr(p.status, 2 | (int)why);
 
@@ -621,39 +633,54 @@ struct FinParams {
 constexpr int kFinWarps = 8;
 
 template <int EPLF, int SE>
-__device__ __forceinline__ void finalize_row(const FinParams& p, int64_t row, int n1, int n2, int lane,
+__device__ __forceinline__ void finalize_row(const FinParams& p, int64_t row, const int (&nl)[kLists], int lane,
                                              uint32_t* bk, int* bi) {
   const int l = (int)(row % p.Tq);
   const int g = ((l / p.rt) * p.rs + p.r0) * p.rt + (l % p.rt);
-  const int n = n1 + n2;
-  const uint64_t* a = p.ws + row * 2 * p.cap;
-  const uint64_t* bsrc = a + p.cap;
-  uint32_t kk[EPLF];
-  int ii[EPLF];
-#pragma unroll
-  for (int t = 0; t < EPLF; ++t) {
-    const int e = t * 32 + lane;
-    uint64_t c = 0;
-    if (e < n1) c = a[e];
-    else if (e < n) c = bsrc[e - n1];
-    kk[t] = (uint32_t)(c >> 32);
-    ii[t] = e < n ? (int)(~(uint32_t)c) : INT_MAX;
-  }
-  int m = n;
-  if (n > p.K) {
-    select_compact<EPLF>(kk, ii, n, p.K, lane, bk, bi);
-    m = p.K;
-  } else {
+  const int e1 = nl[0], e2 = e1 + nl[1], e3 = e2 + nl[2], n = e3 + nl[3];
+  const uint64_t* a = p.ws + row * kLists * p.cap;
+  // The row's concatenated lists are consumed in blocks of up to 32*EPLF entries
+  // together with the running top-K kept in bk/bi (one block in the usual case).
+  int m = 0;   // entries held in bk/bi
+  int e0 = 0;  // next unconsumed list element
+  do {
+    const int take = min(n - e0, EPLF * 32 - m);
+    const int cnt = m + take;
+    uint32_t kk[EPLF];
+    int ii[EPLF];
 #pragma unroll
     for (int t = 0; t < EPLF; ++t) {
       const int e = t * 32 + lane;
-      if (e < n) {
-        bk[e] = kk[t];
-        bi[e] = ii[t];
+      uint64_t c = 0;
+      if (e < m) {
+        c = ((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e]);
+      } else if (e < cnt) {
+        const int x = e0 + e - m;
+        const int li = (x >= e1) + (x >= e2) + (x >= e3);
+        const int off = li == 0 ? 0 : li == 1 ? e1 : li == 2 ? e2 : e3;
+        c = a[li * p.cap + (x - off)];
       }
+      kk[t] = (uint32_t)(c >> 32);
+      ii[t] = e < cnt ? (int)(~(uint32_t)c) : INT_MAX;
     }
     __syncwarp();
-  }
+    if (cnt > p.K) {
+      select_compact<EPLF>(kk, ii, cnt, p.K, lane, bk, bi);
+      m = p.K;
+    } else {
+#pragma unroll
+      for (int t = 0; t < EPLF; ++t) {
+        const int e = t * 32 + lane;
+        if (e < cnt) {
+          bk[e] = kk[t];
+          bi[e] = ii[t];
+        }
+      }
+      __syncwarp();
+      m = cnt;
+    }
+    e0 += take;
+  } while (e0 < n);
   uint64_t cc[SE];
 #pragma unroll
   for (int t = 0; t < SE; ++t) {
@@ -681,14 +708,27 @@ __global__ void __launch_bounds__(kFinWarps * 32, 2) topk_finalize_kernel(const 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kFinWarps + warp;
   if (row >= (int64_t)p.B * p.Tq) return;
-  const int n1 = p.ws_cnt[row * 2], n2 = p.ws_cnt[row * 2 + 1];
+  const int4 c4 = *reinterpret_cast<const int4*>(p.ws_cnt + row * kLists);
+  const int nl[kLists] = {c4.x, c4.y, c4.z, c4.w};
+  const int n = c4.x + c4.y + c4.z + c4.w;
   // with the pair's shared bound a row typically holds 1.1-1.5 K candidates (K <= 128);
-  // the wider forms cover larger K and full workspace slices
-  if (n1 + n2 <= 6 * 32) finalize_row<6, SE>(p, row, n1, n2, lane, skey[warp], sidx[warp]);
-  else if (n1 + n2 <= 12 * 32) finalize_row<12, SE>(p, row, n1, n2, lane, skey[warp], sidx[warp]);
-  else finalize_row<2 * kWcap / 32, SE>(p, row, n1, n2, lane, skey[warp], sidx[warp]);
+  // the wider forms cover larger K and full workspace lists
+  if (n <= 6 * 32) finalize_row<6, SE>(p, row, nl, lane, skey[warp], sidx[warp]);
+  else finalize_row<12, SE>(p, row, nl, lane, skey[warp], sidx[warp]);
 }
 
+#if WF_TOPK_PROF
+}  // namespace
+}  // namespace wf
+extern "C" __attribute__((visibility("default"))) int wf_debug_topk_prof(unsigned long long* out16) {
+  cudaError_t e = cudaMemcpyFromSymbol(out16, wf::g_topk_prof, sizeof(unsigned long long) * 16);
+  unsigned long long z[16] = {};
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(wf::g_topk_prof, z, sizeof(z));
+  return (int)e;
+}
+namespace wf {
+namespace {
+#endif
 // ---------------------------------------------------------------- host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -767,10 +807,10 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
   t.idx = p.idx;
   t.status = p.status;
   const size_t rows = (size_t)p.B * p.Tq;
-  const size_t need = rows * 2 * kWcap * sizeof(uint64_t) + rows * 2 * sizeof(int32_t);
+  const size_t need = rows * kLists * kWcap * sizeof(uint64_t) + rows * kLists * sizeof(int32_t);
   if (!p.ws || p.ws_bytes < need || reinterpret_cast<uintptr_t>(p.ws) % 16) return -3;
   t.ws = reinterpret_cast<uint64_t*>(p.ws);
-  t.ws_cnt = reinterpret_cast<int32_t*>(t.ws + rows * 2 * kWcap);
+  t.ws_cnt = reinterpret_cast<int32_t*>(t.ws + rows * kLists * kWcap);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * ((p.Tq + kM - 1) / kM), p.B);
@@ -834,7 +874,7 @@ bool topk_tc_supported(const TopkParams& p, int dtype) {
 size_t topk_tc_workspace_bytes(int64_t B, int64_t Tq, int K) {
   if (K > 128) return 0;
   const size_t rows = (size_t)B * Tq;
-  return rows * 2 * kWcap * sizeof(uint64_t) + rows * 2 * sizeof(int32_t);
+  return rows * kLists * kWcap * sizeof(uint64_t) + rows * kLists * sizeof(int32_t);
 }
 
 int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream) {
@@ -849,7 +889,7 @@ int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream) {
 // kNoAllocScratchBytes for it until the process exits.  All calls share it and it
 // keeps the previous call's contents; nothing in it needs to start at zero,
 // because the retrieval kernel writes every count and candidate it later reads.
-constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB: B*Tq <= 2044 query rows (4104 bytes each) for K <= 128
+constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB: B*Tq <= 2044 query rows (8208 bytes each) for K <= 128
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
