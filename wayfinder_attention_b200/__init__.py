@@ -16,8 +16,10 @@ from .attention import (
     LearnedAddressModule,
     LearnedAddressSparseAttention,
     RetrievalConfig,
+    RoutingSparseAttention,
     retrieval_config_from_dict,
 )
+from .router import MultiScaleRouter, PerLayerRouter, RouterMLP
 from .causal_topk import causal_topk, causal_topk_available, promote_compute_dtype
 from .decoder import DenseSDPAAttention, TransformerBlock, TransformerLM
 from .host_pipeline import HostFusedSparseAttention, host_fused_sparse_attention
@@ -42,6 +44,10 @@ __all__ = [
     "LearnedAddressModule",
     "LearnedAddressSparseAttention",
     "KeyVectorSparseAttention",
+    "RoutingSparseAttention",
+    "RouterMLP",
+    "PerLayerRouter",
+    "MultiScaleRouter",
     "RetrievalConfig",
     "retrieval_config_from_dict",
     "DenseSDPAAttention",

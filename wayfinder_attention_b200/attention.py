@@ -257,3 +257,100 @@ class KeyVectorSparseAttention(nn.Module):
                 attn_dense.scatter_(2, idx, 1.0 / k_eff)
             return out, attn_dense
         return out
+
+
+class RoutingSparseAttention(nn.Module):
+    """Router-driven sparse attention (``routing_attention/models/attention.py:504-617``).
+
+    The router's (B, T, R) routing vectors are the search vectors of the same fused
+    retrieval + sparse-attention kernels: ``RouterMLP.forward_query_key`` (or
+    ``PerLayerRouter`` for ``layer_idx``, or the concatenated local + global vectors
+    of a ``MultiScaleRouter``, R = 2 * routing_dim).  Same constructor, submodule
+    names (``router``, ``q_proj``, ``k_proj``, ``v_proj``, ``out_proj``,
+    ``_key_baseline``) and ``forward`` contract as the reference.  The non-fused
+    path rounds the routing vectors to ``retrieval_config.dtype`` before retrieval
+    (the ``RoutingRetriever`` numerics), except with a ``MultiScaleRouter``, whose
+    ``retrieve_indices`` merges the two routers' candidates as the reference does.
+    Per-head routing vectors (B, T, H, R) are rejected with ``ValueError`` on the
+    fused path, as the reference operator rejects non-3-D search vectors.
+    """
+
+    def __init__(
+        self,
+        d_model: int,
+        n_heads: int,
+        router: nn.Module,
+        top_k: int = 32,
+        dropout: float = 0.1,
+        layer_idx: int = 0,
+        retrieval_mode: Literal["routing", "key_vector"] = "routing",
+        retrieval_config: RetrievalConfig | dict | None = None,
+        pad_mode: str = "reference",
+    ):
+        super().__init__()
+        assert d_model % n_heads == 0
+        self.n_heads = n_heads
+        self.head_dim = d_model // n_heads
+        self.scale = self.head_dim ** -0.5
+        self.top_k = top_k
+        self.router = router
+        self.layer_idx = layer_idx
+        self.retrieval_mode = retrieval_mode
+        self.pad_mode = pad_mode
+        self._retrieval_cfg = _resolve_retrieval_cfg(retrieval_config, top_k)
+        self.q_proj = nn.Linear(d_model, d_model)
+        self.k_proj = nn.Linear(d_model, d_model)
+        self.v_proj = nn.Linear(d_model, d_model)
+        self.out_proj = nn.Linear(d_model, d_model)
+        self.dropout = nn.Dropout(dropout)
+        if retrieval_mode == "key_vector":
+            self._key_baseline = KeyVectorSparseAttention(d_model, n_heads, top_k, dropout,
+                                                          retrieval_config=retrieval_config, pad_mode=pad_mode)
+
+    def _get_query_key_routing(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        from .router import PerLayerRouter
+
+        if isinstance(self.router, PerLayerRouter):
+            return self.router.get_router(self.layer_idx).forward_query_key(x)
+        if hasattr(self.router, "forward_query_key"):
+            return self.router.forward_query_key(x)
+        r = self.router(x)
+        return r, r
+
+    def forward(self, x: torch.Tensor, attn_mask: Optional[torch.Tensor] = None, return_attention: bool = False,
+                precomputed_routing: Optional[torch.Tensor] = None):
+        from .router import MultiScaleRouter
+
+        if self.retrieval_mode == "key_vector":
+            return self._key_baseline(x, attn_mask=attn_mask, return_attention=return_attention)
+        B, T, D = x.shape
+        q = self.q_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
+        k = self.k_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
+        v = self.v_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
+        if self._retrieval_cfg.use_fused_sparse:
+            q_r, k_r = self._get_query_key_routing(x)
+            meat, candidate_idx = fused_sparse_attention(q_r, k_r, q, k, v, self.top_k, self.scale,
+                                                         pad_mode=self.pad_mode)
+        else:
+            if self.training and self.dropout.p > 0:
+                raise NotImplementedError(
+                    "attention-probability dropout of the non-fused path is not implemented "
+                    "(forward-only kernels); use eval() or retrieval_config.use_fused_sparse=True"
+                )
+            if isinstance(self.router, MultiScaleRouter):
+                candidate_idx = self.router.retrieve_indices(x, self.top_k, self.layer_idx).to(torch.int32)
+            else:
+                q_r, k_r = self._get_query_key_routing(x)
+                rdt = _DTYPES.get(self._retrieval_cfg.dtype, torch.float16)
+                candidate_idx = causal_topk(q_r.to(rdt), k_r.to(rdt), self.top_k, pad_mode=self.pad_mode)
+            meat = sparse_meat_attention(q, k, v, candidate_idx, self.scale, mask_negative=self.pad_mode == "masked")
+        out = self.out_proj(meat.transpose(1, 2).contiguous().view(B, T, D))
+        if return_attention:
+            k_eff = candidate_idx.shape[-1]
+            attn_dense = torch.zeros(B, T, T, device=x.device)
+            if k_eff > 0:
+                idx = candidate_idx.long()
+                idx = torch.where(idx >= 0, idx, idx[..., :1])
+                attn_dense.scatter_(2, idx, 1.0 / k_eff)
+            return out, attn_dense
+        return out
