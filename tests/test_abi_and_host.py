@@ -154,4 +154,9 @@ def test_workspace_query():
     assert lib.wf_causal_topk_workspace_bytes(1, 16384, 16384, 32, 128, _lib.WF_DTYPE_BF16) == 16384 * (4 * 256 * 8 + 16)
     assert lib.wf_causal_topk_workspace_bytes(2, 100, 100, 32, 64, _lib.WF_DTYPE_F16) == 200 * (4 * 256 * 8 + 16)
     assert lib.wf_causal_topk_workspace_bytes(1, 2048, 2048, 32, 128, _lib.WF_DTYPE_F32) == 0  # CUDA-core path
-    assert lib.wf_causal_topk_workspace_bytes(1, 2048, 2048, 32, 256, _lib.WF_DTYPE_BF16) == 0
+    # K <= 256 on tensor cores: lists of 384 slots above K = 128
+    assert lib.wf_causal_topk_workspace_bytes(1, 2048, 2048, 32, 256, _lib.WF_DTYPE_BF16) == 2048 * (4 * 384 * 8 + 16)
+    # large batches run in slices of 65536 // T batch elements that reuse one workspace
+    assert lib.wf_causal_topk_workspace_bytes(64, 8192, 8192, 32, 128, _lib.WF_DTYPE_BF16) == 8 * 8192 * (4 * 256 * 8 + 16)
+    assert lib.wf_causal_topk_workspace_bytes(1, 65536, 65536, 32, 128, _lib.WF_DTYPE_BF16) == 65536 * (4 * 256 * 8 + 16)
+    assert lib.wf_causal_topk_workspace_bytes(1, 2048, 2048, 32, 300, _lib.WF_DTYPE_BF16) == 0  # CUDA-core path

@@ -348,6 +348,10 @@ def test_decoder_prefill_smoke(cuda_device):
         (32, 32, 777, 3, torch.bfloat16, True),
         (32, 1, 300, 1, torch.bfloat16, False),
         (32, 128, 130, 1, torch.bfloat16, False),
+        (32, 256, 8192, 2, torch.bfloat16, True),   # K = 256: 384-slot lists, 8-register sort
+        (64, 200, 2500, 1, torch.float16, False),
+        (32, 256, 300, 1, torch.bfloat16, False),   # short rows: K_eff = 256 with pads
+        (32, 128, 8192, 10, torch.bfloat16, True),  # 8 + 2 batch elements: two workspace slices
     ],
 )
 def test_tensor_core_topk_equals_cuda_core(R, K, T, B, dtype, clustered, cuda_device, monkeypatch):

@@ -8,30 +8,33 @@
 // Work split.  A tile of 128 query rows (the 128 TMEM lanes) is handled by a
 // cluster of two CTAs on two SMs; CTA rank r streams the key chunks c = r, r+2,
 // ... (128 keys each), so the long rows at the end of the causal triangle are
-// shared by two SMs.  Each CTA has 5 warps: warp 4 TMA-loads the q tile and the
+// shared by two SMs.  Each CTA has 9 warps: warp 8 TMA-loads the q tile and the
 // key chunks into a shared-memory ring and one of its lanes issues tcgen05.mma
 // (M=128, N=128, K=16 per instruction, fp32 accumulate) into a 2-deep TMEM
-// accumulator ring; warps 0-3 own one query row per thread.
+// accumulator ring; warps 0-7 are two per TMEM lane quadrant: thread t of warp w
+// owns query row 32*(w%4)+t and the column half w/4 of every chunk.
 //
 // Selection is two passes over the CTA's chunks (the MMAs are recomputed; they
 // are nearly free):
 //   pass 1  each thread keeps, in 256 TMEM columns of its lane, the maximum
-//           tensor-core score of each of 256 key groups (group = key position
-//           within a 256-key window of the CTA's stream).  The K-th largest of
-//           those 256 group maxima is the score of K distinct keys, so it lower-
-//           bounds the row's K-th best score.  The two CTAs exchange this bound
-//           through distributed shared memory and keep the larger.
+//           tensor-core score of each of 256 key groups (column x parity of the
+//           chunk in the CTA's stream).  The K-th largest of the pair's 512 group
+//           maxima is the score of K distinct keys, so it lower-bounds the row's
+//           K-th best score; the two CTAs bisect it together (7 steps, counts
+//           exchanged through distributed shared memory).
 //   pass 2  a key is admitted when its tensor-core score reaches
-//           (bound - margin); about 1.4 K keys per row are admitted.  Admitted
+//           (bound - margin); about 75 keys per row and CTA at K = 128.  Admitted
 //           keys are queued per warp and rescored exactly in fp32 by all 32
 //           lanes together (sequential FMA over d from the q tile and the staged
-//           key rows: the arithmetic of the CUDA-core kernel), then appended to
-//           the row's candidate buffer.  A full buffer is compacted to its exact
-//           top-K (warp radix select), which raises the admission threshold.
-//   output  rescored candidates go straight to a caller-provided workspace
-//           (256 slots per row and CTA; a full slice is compacted to its exact top-K); topk_finalize_kernel, launched right
-//           after at full occupancy (one warp per row), selects the exact top-K
-//           of the two lists, sorts it and writes the indices and pads.
+//           key rows: the arithmetic of the CUDA-core kernel).
+//   output  rescored candidates go straight to a caller-provided workspace, one
+//           list of KW slots per (row, CTA, warp) with the count in a register
+//           (KW = 256 for K <= 128, 384 for K <= 256); a list within 64 of full
+//           is compacted to its exact top-K (warp radix select), which raises the
+//           row's admission threshold.  topk_finalize_kernel, launched right after
+//           at full occupancy (one warp per row), selects the exact top-K of the
+//           four lists, sorts it and writes the indices and pads.  Batches larger
+//           than about 65536 query rows run in slices that reuse the workspace.
 // The margin, 2^-13 * sum_d |q_d| * max|k|, exceeds any plausible accumulation
 // error of a 32-term fp32 dot product with exact bf16/fp16 products, so every
 // key whose exact score reaches the K-th best is admitted: the result is exact
@@ -59,7 +62,10 @@ constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant
 constexpr int kThreads = (kEpiWarps + 1) * 32;
 constexpr int kGroups = 256;  // pass-1 key groups per row (TMEM columns 256..511)
 constexpr int kQcap = 2048;   // rescoring queue entries per warp (one chunk admits at most 64 x 32)
-constexpr int kWcap = 256;    // workspace candidates per (row, CTA, warp); a full list is compacted to its top-K
+// Workspace list capacity KW per (row, CTA, warp) is a template parameter: 256 for
+// K <= 128 and 384 for K <= 256 (a list within 64 of full is compacted to its top-K,
+// which leaves room for the next chunk).
+constexpr int kRowsPerPass = 65536;  // query rows per launch pair; larger batches run in slices
 constexpr int kLists = 4;     // candidate lists per row: 2 CTAs x 2 selection warps
 constexpr unsigned kFullMask = 0xffffffffu;
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
@@ -90,7 +96,7 @@ struct TcParams {
   int rt, rs, r0;
   int32_t* idx;
   int32_t* status;
-  uint64_t* ws;      // [B*Tq][kLists][kWcap] candidate composites (key << 32 | ~index)
+  uint64_t* ws;      // [B*Tq][kLists][KW] candidate composites (key << 32 | ~index)
   int32_t* ws_cnt;   // [B*Tq][kLists] candidate counts
 };
 
@@ -98,8 +104,9 @@ __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + 
 
 constexpr int kXRounds = 8;  // pair exchanges for the bound: extrema + 7 bisection steps
 
-template <int R, int EPL>
+template <int R, int KW>
 struct Layout {
+  static constexpr int KB = KW - 128;  // merge buffer entries per warp (>= K)
   static constexpr int ROWB = R * 2;
   static constexpr int S = R >= 64 ? 2 : 3;  // shared-memory stages
   static constexpr size_t Q_BYTES = (size_t)kM * ROWB;
@@ -114,8 +121,8 @@ struct Layout {
   static constexpr size_t off_xslot = align_up(off_misc + 16, 16);  // [2 parities][kM rows][4] bisection exchange
   static constexpr size_t off_xpair = off_xslot + 4 * 2 * kM * 4;  // [2 parities][2 warps][kM][4] pair sums
   static constexpr size_t off_queue = off_xpair + 4 * 2 * 2 * kM * 4;
-  static constexpr size_t off_merge = off_queue + 4 * (size_t)kQcap * kEpiWarps;  // per warp: K keys + K indices
-  static constexpr size_t bytes = off_merge + (size_t)kEpiWarps * 128 * (4 + 4);
+  static constexpr size_t off_merge = off_queue + 4 * (size_t)kQcap * kEpiWarps;  // per warp: KB keys + KB indices
+  static constexpr size_t bytes = off_merge + (size_t)kEpiWarps * KB * (4 + 4);
   // Slack to align the dynamic base to 1024, and at least 116 KB in total: two of
   // these CTAs must never share an SM (each allocates all 512 TMEM columns), while
   // sparse-attention blocks (37 KB) may run beside one.
@@ -156,11 +163,12 @@ __device__ __forceinline__ float dot_swizzled(const unsigned char* qtile, int qr
   return acc;
 }
 
-template <typename TI, int R, int EPL, int SE, int EPLF>
+template <typename TI, int R, int KW>
 __global__ void __launch_bounds__(kThreads, 1)
     causal_topk_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                           const TcParams p) {
-  using L = Layout<R, EPL>;
+  using L = Layout<R, KW>;
+  constexpr int KB = L::KB;
   constexpr int S = L::S;
   constexpr int ROWB = L::ROWB;
   constexpr int KSTEPS = R / 16;
@@ -187,8 +195,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* queues = reinterpret_cast<uint32_t*>(base + L::off_queue);
   uint32_t* xslot = reinterpret_cast<uint32_t*>(base + L::off_xslot);
   uint32_t* xpair = reinterpret_cast<uint32_t*>(base + L::off_xpair);
-  uint32_t* mkey = reinterpret_cast<uint32_t*>(base + L::off_merge);       // [warp][128]
-  int* midx = reinterpret_cast<int*>(mkey + kEpiWarps * 128);              // [warp][128]
+  uint32_t* mkey = reinterpret_cast<uint32_t*>(base + L::off_merge);       // [warp][KB]
+  int* midx = reinterpret_cast<int*>(mkey + kEpiWarps * KB);               // [warp][KB]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -490,7 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ent = queue[e];
         const int lr = ent & 31, jj = (ent >> 5) & 127, dest = (int)(ent >> 12);
         const float ex = dot_swizzled<TI, ROWB>(qs, 32 * qd + lr, stage, jj);
-        p.ws[(((row0 + lr) * 2 + rank) * 2 + hf) * kWcap + dest] =
+        p.ws[(((row0 + lr) * 2 + rank) * 2 + hf) * KW + dest] =
             ((uint64_t)ordered_key(ex) << 32) | (uint32_t)(~(uint32_t)(c * kN + jj));
       }
       __syncwarp();
@@ -536,26 +544,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int np = __popc(masks[0]) + __popc(masks[1]);
       // A list that this chunk could overflow is compacted to its exact top-K first
       // (queued entries written out beforehand); that also raises the row's threshold.
-      unsigned need = __ballot_sync(kFullMask, cnt + np > kWcap);
+      unsigned need = __ballot_sync(kFullMask, cnt + np > KW);
       if (need) {
         flush(stage, c);
-        uint32_t* bk = mkey + warp * 128;
-        int* bi = midx + warp * 128;
+        uint32_t* bk = mkey + warp * KB;
+        int* bi = midx + warp * KB;
         while (need) {
           const int ln = __ffs(need) - 1;
           need &= need - 1;
           const int n = __shfl_sync(kFullMask, cnt, ln);
-          uint64_t* wrow = p.ws + (((row0 + ln) * 2 + rank) * 2 + hf) * kWcap;
-          uint32_t kk[kWcap / 32];
-          int ii[kWcap / 32];
+          uint64_t* wrow = p.ws + (((row0 + ln) * 2 + rank) * 2 + hf) * KW;
+          uint32_t kk[KW / 32];
+          int ii[KW / 32];
 #pragma unroll
-          for (int t = 0; t < kWcap / 32; ++t) {
+          for (int t = 0; t < KW / 32; ++t) {
             const int e = t * 32 + lane;
             const uint64_t cv = e < n ? wrow[e] : 0ull;
             kk[t] = (uint32_t)(cv >> 32);
             ii[t] = e < n ? (int)(~(uint32_t)cv) : INT_MAX;
           }
-          const uint32_t tau = select_compact<kWcap / 32>(kk, ii, n, p.K, lane, bk, bi);
+          const uint32_t tau = select_compact<KW / 32>(kk, ii, n, p.K, lane, bk, bi);
           for (int e = lane; e < p.K; e += 32) wrow[e] = ((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e]);
           __syncwarp();
           if (lane == ln) {
@@ -701,20 +709,21 @@ __device__ __forceinline__ void finalize_row(const FinParams& p, int64_t row, co
   }
 }
 
-template <int SE>
+template <int SE, int KB>
 __global__ void __launch_bounds__(kFinWarps * 32, 2) topk_finalize_kernel(const FinParams p) {
-  __shared__ uint32_t skey[kFinWarps][128];
-  __shared__ int sidx[kFinWarps][128];
+  __shared__ uint32_t skey[kFinWarps][KB];
+  __shared__ int sidx[kFinWarps][KB];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kFinWarps + warp;
   if (row >= (int64_t)p.B * p.Tq) return;
   const int4 c4 = *reinterpret_cast<const int4*>(p.ws_cnt + row * kLists);
   const int nl[kLists] = {c4.x, c4.y, c4.z, c4.w};
   const int n = c4.x + c4.y + c4.z + c4.w;
-  // with the pair's shared bound a row typically holds 1.1-1.5 K candidates (K <= 128);
-  // the wider forms cover larger K and full workspace lists
-  if (n <= 6 * 32) finalize_row<6, SE>(p, row, nl, lane, skey[warp], sidx[warp]);
-  else finalize_row<12, SE>(p, row, nl, lane, skey[warp], sidx[warp]);
+  // with the pair's shared bound a row typically holds 1.1-1.5 K candidates; the wider
+  // form merges larger rows in blocks (it must hold more than KB entries to progress)
+  constexpr int E1 = KB <= 128 ? 6 : 12, E2 = KB <= 128 ? 12 : 16;
+  if (n <= E1 * 32) finalize_row<E1, SE>(p, row, nl, lane, skey[warp], sidx[warp]);
+  else finalize_row<E2, SE>(p, row, nl, lane, skey[warp], sidx[warp]);
 }
 
 #if WF_TOPK_PROF
@@ -767,7 +776,7 @@ bool make_map(CUtensorMap* map, const void* ptr, bool bf16, int R, int64_t T, in
 
 template <int R>
 size_t smem_for_k(int K) {
-  return K <= 128 ? Layout<R, 1>::smem : 0;
+  return K <= 128 ? Layout<R, 256>::smem : K <= 256 ? Layout<R, 384>::smem : 0;
 }
 
 size_t tc_smem(int R, int K) {
@@ -779,11 +788,21 @@ size_t tc_smem(int R, int K) {
   }
 }
 
-template <typename TI, int R, int EPL, int SE, int EPLF>
+int list_capacity(int K) { return K <= 128 ? 256 : 384; }
+
+// Batch elements per launch pair: the workspace holds about kRowsPerPass query rows.
+int64_t batch_per_pass(int64_t B, int64_t Tq) {
+  const int64_t bpp = Tq >= kRowsPerPass ? 1 : kRowsPerPass / Tq;
+  return bpp < B ? bpp : B;
+}
+
+size_t ws_bytes_per_row(int K) { return (size_t)kLists * list_capacity(K) * sizeof(uint64_t) + kLists * sizeof(int32_t); }
+
+template <typename TI, int R, int KW, int SE>
 int launch_t(const TopkParams& p, cudaStream_t stream) {
-  using L = Layout<R, EPL>;
+  using L = Layout<R, KW>;
   if (L::smem > kMaxSmem) return -1;
-  auto kern = causal_topk_tc_kernel<TI, R, EPL, SE, EPLF>;
+  auto kern = causal_topk_tc_kernel<TI, R, KW>;
   static bool configured[kMaxDevices] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -794,54 +813,68 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
     if (dev < kMaxDevices) configured[dev] = true;
   }
   const bool bf16 = !std::is_same<TI, __half>::value;
-  CUtensorMap qmap, kmap;
-  if (!make_map(&qmap, p.q, bf16, R, p.Tq, p.B, p.qst, p.qsb, kM)) return -1;
-  if (!make_map(&kmap, p.k, bf16, R, p.Tk, p.B, p.kst, p.ksb, kN)) return -1;
-  TcParams t{};
-  t.q = p.q;
-  t.qsb = p.qsb;
-  t.qst = p.qst;
-  t.B = p.B; t.Tq = p.Tq; t.Tk = p.Tk; t.K = p.K;
-  t.pad_mode = p.pad_mode;
-  t.rt = p.rt; t.rs = p.rs; t.r0 = p.r0;
-  t.idx = p.idx;
-  t.status = p.status;
-  const size_t rows = (size_t)p.B * p.Tq;
-  const size_t need = rows * kLists * kWcap * sizeof(uint64_t) + rows * kLists * sizeof(int32_t);
+  const int64_t bpp = batch_per_pass(p.B, p.Tq);
+  const size_t rows_pass = (size_t)bpp * p.Tq;
+  const size_t need = rows_pass * ws_bytes_per_row(p.K);
   if (!p.ws || p.ws_bytes < need || reinterpret_cast<uintptr_t>(p.ws) % 16) return -3;
-  t.ws = reinterpret_cast<uint64_t*>(p.ws);
-  t.ws_cnt = reinterpret_cast<int32_t*>(t.ws + rows * kLists * kWcap);
+  uint64_t* ws = reinterpret_cast<uint64_t*>(p.ws);
+  int32_t* ws_cnt = reinterpret_cast<int32_t*>(ws + rows_pass * kLists * KW);
+  const size_t esz = 2;
+  // Batch slices run one after the other on the stream and reuse the workspace.
+  for (int64_t b0 = 0; b0 < p.B; b0 += bpp) {
+    const int nb = (int)(p.B - b0 < bpp ? p.B - b0 : bpp);
+    const void* q = static_cast<const char*>(p.q) + (size_t)(b0 * p.qsb) * esz;
+    const void* k = static_cast<const char*>(p.k) + (size_t)(b0 * p.ksb) * esz;
+    CUtensorMap qmap, kmap;
+    if (!make_map(&qmap, q, bf16, R, p.Tq, nb, p.qst, p.qsb, kM)) return -1;
+    if (!make_map(&kmap, k, bf16, R, p.Tk, nb, p.kst, p.ksb, kN)) return -1;
+    TcParams t{};
+    t.q = q;
+    t.qsb = p.qsb;
+    t.qst = p.qst;
+    t.B = nb; t.Tq = p.Tq; t.Tk = p.Tk; t.K = p.K;
+    t.pad_mode = p.pad_mode;
+    t.rt = p.rt; t.rs = p.rs; t.r0 = p.r0;
+    t.idx = p.idx + (size_t)b0 * p.Tq * p.K;
+    t.status = p.status;
+    t.ws = ws;
+    t.ws_cnt = ws_cnt;
 
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * ((p.Tq + kM - 1) / kM), p.B);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = L::smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kern, qmap, kmap, t);
-  if (e != cudaSuccess) return (int)e;
-  FinParams f{};
-  f.ws = t.ws;
-  f.ws_cnt = t.ws_cnt;
-  f.idx = p.idx;
-  f.B = p.B; f.Tq = p.Tq; f.Tk = p.Tk; f.K = p.K; f.cap = kWcap;
-  f.pad_mode = p.pad_mode;
-  f.rt = p.rt; f.rs = p.rs; f.r0 = p.r0;
-  topk_finalize_kernel<SE><<<(unsigned)((rows + kFinWarps - 1) / kFinWarps), kFinWarps * 32, 0, stream>>>(f);
-  return (int)cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * ((p.Tq + kM - 1) / kM), nb);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, qmap, kmap, t);
+    if (e != cudaSuccess) return (int)e;
+    FinParams f{};
+    f.ws = ws;
+    f.ws_cnt = ws_cnt;
+    f.idx = t.idx;
+    f.B = nb; f.Tq = p.Tq; f.Tk = p.Tk; f.K = p.K; f.cap = KW;
+    f.pad_mode = p.pad_mode;
+    f.rt = p.rt; f.rs = p.rs; f.r0 = p.r0;
+    const size_t rows = (size_t)nb * p.Tq;
+    topk_finalize_kernel<SE, KW - 128><<<(unsigned)((rows + kFinWarps - 1) / kFinWarps), kFinWarps * 32, 0, stream>>>(f);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+  }
+  return 0;
 }
 
 template <typename TI, int R>
 int launch_r(const TopkParams& p, cudaStream_t s) {
-  if (p.K <= 32) return launch_t<TI, R, 4, 1, 2>(p, s);
-  if (p.K <= 64) return launch_t<TI, R, 5, 2, 4>(p, s);
-  if (p.K <= 128) return launch_t<TI, R, 7, 4, 8>(p, s);
+  if (p.K <= 32) return launch_t<TI, R, 256, 1>(p, s);
+  if (p.K <= 64) return launch_t<TI, R, 256, 2>(p, s);
+  if (p.K <= 128) return launch_t<TI, R, 256, 4>(p, s);
+  if (p.K <= 256) return launch_t<TI, R, 384, 8>(p, s);
   return -1;
 }
 
@@ -860,7 +893,7 @@ int launch_ti(const TopkParams& p, cudaStream_t s) {
 bool topk_tc_supported(const TopkParams& p, int dtype) {
   if (dtype != kBF16 && dtype != kF16) return false;
   if (p.R != 16 && p.R != 32 && p.R != 64) return false;
-  if (p.K > 128 || p.Tk > 65536 || p.B > 65535) return false;
+  if (p.K > 256 || p.Tk > 65536 || p.B > 65535) return false;
   const size_t sm = tc_smem(p.R, p.K);
   if (sm == 0 || sm > kMaxSmem) return false;
   if (p.qsr != 1 || p.ksr != 1) return false;
@@ -872,9 +905,8 @@ bool topk_tc_supported(const TopkParams& p, int dtype) {
 }
 
 size_t topk_tc_workspace_bytes(int64_t B, int64_t Tq, int K) {
-  if (K > 128) return 0;
-  const size_t rows = (size_t)B * Tq;
-  return rows * kLists * kWcap * sizeof(uint64_t) + rows * kLists * sizeof(int32_t);
+  if (K > 256 || B <= 0 || Tq <= 0) return 0;
+  return (size_t)batch_per_pass(B, Tq) * Tq * ws_bytes_per_row(K);
 }
 
 int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream) {

@@ -67,6 +67,8 @@ CONFIGS = {
     "cfg3_layer": Workload("cfg3_layer", 8, 4, 4096, 64, 32, 128, torch.bfloat16),
     "cfg4": Workload("cfg4", 1, 32, 65536, 128, 32, 128, torch.bfloat16),
     "cfg5": Workload("cfg5", 64, 16, 8192, 64, 32, 128, torch.bfloat16, clustered=True),
+    "cfg5_k64": Workload("cfg5_k64", 64, 16, 8192, 64, 32, 64, torch.bfloat16, clustered=True),
+    "cfg5_k256": Workload("cfg5_k256", 64, 16, 8192, 64, 32, 256, torch.bfloat16, clustered=True),
 }
 
 
