@@ -12,6 +12,7 @@
  *   wf_sparse_attention       <- routing_attention/kernels/fused_sparse.py:275-324  sparse_meat_attention()
  *   wf_fused_sparse_attention <- routing_attention/kernels/fused_sparse.py:327-356  fused_sparse_attention()
  *   wf_fused_sparse_attention_host: the same operator on host-resident tensors (copies overlapped)
+ *   wf_address_projection     <- routing_attention/models/learned_address.py:39-46  forward_query_key()
  */
 #ifndef WAYFINDER_H_
 #define WAYFINDER_H_
@@ -207,6 +208,26 @@ WF_API int wf_fused_sparse_attention_host(const void* q_addr_h, const void* k_ad
                                           void* d_q_addr, void* d_k_addr, void* d_q, void* d_k, void* d_v,
                                           int32_t* d_idx, void* d_out, void* workspace, size_t workspace_bytes,
                                           int32_t* status, void* stream, void* h2d_stream, void* d2h_stream);
+
+/*
+ * Fused learned-address projection.  Replaces LearnedAddressModule.forward_query_key
+ * (routing_attention/models/learned_address.py:39-46: nn.Linear(d_model, d_A) for the
+ * query and the key address, then F.normalize(dim=-1) on each) with one pass over x:
+ *   out[m, n] = (x[m, :] . w[n, :] + bias[n]), then every consecutive `group` outputs
+ *   are divided by max(||.||_2, 1e-12) when `normalize` is nonzero.
+ * Stack the query and key weights ([W_q; W_k], n_out = 2 * d_A, group = d_A) to get
+ * both addresses at once.
+ *   x    : (M, d_model) rows of x_row_stride elements, dtype WF_DTYPE_*
+ *   w    : (n_out, d_model) contiguous, same dtype; bias: (n_out) same dtype or NULL
+ *   out  : (M, n_out) rows of out_row_stride elements, same dtype
+ * bf16/fp16 with n_out in {32, 64, 128} run on tcgen05 (fp32 accumulate, fp32
+ * normalisation, one rounding); fp32 and other widths on CUDA cores in fp32.
+ * group: power of two <= 32 dividing n_out; n_out: a divisor of 32 or a multiple
+ * of 32 up to 256.
+ */
+WF_API int wf_address_projection(const void* x, int32_t dtype, int64_t M, int32_t d_model, int64_t x_row_stride,
+                                 const void* w, const void* bias, int32_t n_out, int32_t group, int32_t normalize,
+                                 void* out, int64_t out_row_stride, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

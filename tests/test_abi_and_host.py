@@ -86,6 +86,21 @@ def test_host_pipeline_entry_validates_before_enqueueing():
     assert call(qs=bad) == _lib.WF_ERR_UNSUPPORTED and b"stride" in lib.wf_last_error()
 
 
+def test_address_projection_entry_validates_before_launch():
+    lib = _lib.load_library()
+    p = ctypes.c_void_p(4096)
+
+    def call(n_out=64, group=32, d_model=256, dtype=0, xs=256):
+        return lib.wf_address_projection(p, dtype, 100, d_model, xs, p, None, n_out, group, 1, p, n_out, None, None)
+
+    assert call(group=24) == _lib.WF_ERR_INVALID_ARGUMENT and b"group" in lib.wf_last_error()
+    assert call(group=64) == _lib.WF_ERR_INVALID_ARGUMENT
+    assert call(n_out=48, group=16) == _lib.WF_ERR_UNSUPPORTED and b"n_out" in lib.wf_last_error()
+    assert call(xs=100) == _lib.WF_ERR_INVALID_ARGUMENT and b"stride" in lib.wf_last_error()
+    assert call(dtype=9) == _lib.WF_ERR_INVALID_ARGUMENT
+    assert lib.wf_address_projection(None, 0, 0, 256, 256, None, None, 64, 32, 1, None, 64, None, None) == _lib.WF_OK
+
+
 def test_python_api_validates_like_reference():
     a = torch.zeros(1, 8, 32)
     with pytest.raises(ValueError, match="shape mismatch"):

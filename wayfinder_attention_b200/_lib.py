@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "wf_sparse_attention_cyclic_kv",
     "wf_fused_sparse_attention",
     "wf_fused_sparse_attention_host",
+    "wf_address_projection",
 )
 
 _DTYPE_CODES = {
@@ -95,6 +96,10 @@ def _declare(lib: ctypes.CDLL) -> None:
         _vp, _vp, _i32, _i32, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i32, _i64p, _i64p, _i64p,
         _i32, _f32, _i32, _i32, _vp, _vp, _i32, _i64p,
         _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp, _vp, _vp, _vp,
+    ]
+    lib.wf_address_projection.restype = ctypes.c_int
+    lib.wf_address_projection.argtypes = [
+        _vp, _i32, _i64, _i32, _i64, _vp, _vp, _i32, _i32, _i32, _vp, _i64, _vp, _vp,
     ]
 
 

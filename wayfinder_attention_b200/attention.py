@@ -84,13 +84,35 @@ class LearnedAddressModule(nn.Module):
         self.normalize = normalize
         self.q_addr_proj = nn.Linear(d_model, address_dim)
         self.k_addr_proj = nn.Linear(d_model, address_dim) if similarity == "asymmetric" else None
+        # inference on CUDA: both projections + normalisation in one kernel (wf_address_projection)
+        self.fused_projection = True
 
     def forward_query_key(self, hidden: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        if self._use_fused_projection(hidden):
+            return self._fused_query_key(hidden)
         q = self.q_addr_proj(hidden)
         k = self.k_addr_proj(hidden) if self.k_addr_proj is not None else q
         if self.normalize:
             q = F.normalize(q, dim=-1)
             k = F.normalize(k, dim=-1)
+        return q, k
+
+    def _use_fused_projection(self, hidden: torch.Tensor) -> bool:
+        """One fused kernel (``wf_address_projection``) when no gradient is needed."""
+        if not (self.fused_projection and hidden.is_cuda) or hidden.dtype not in _DTYPES.values():
+            return False
+        return not (torch.is_grad_enabled() and (hidden.requires_grad or any(p.requires_grad for p in self.parameters())))
+
+    def _fused_query_key(self, hidden: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        from .address_projection import StackedAddressWeights, address_projection
+
+        if not hasattr(self, "_stacked"):
+            self._stacked = StackedAddressWeights()
+        layers = [self.q_addr_proj] + ([self.k_addr_proj] if self.k_addr_proj is not None else [])
+        w, b = self._stacked.get(layers)
+        out = address_projection(hidden, w, b, self.address_dim, normalize=self.normalize)
+        q = out[..., : self.address_dim]
+        k = out[..., self.address_dim:] if self.k_addr_proj is not None else q
         return q, k
 
     def forward(self, hidden: torch.Tensor) -> torch.Tensor:

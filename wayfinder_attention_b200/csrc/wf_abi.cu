@@ -428,4 +428,26 @@ int wf_fused_sparse_attention_host(const void* q_addr_h, const void* k_addr_h, i
   return ok();
 }
 
+
+int wf_address_projection(const void* x, int32_t dtype, int64_t M, int32_t d_model, int64_t x_row_stride,
+                          const void* w, const void* bias, int32_t n_out, int32_t group, int32_t normalize,
+                          void* out, int64_t out_row_stride, int32_t* status, void* stream) {
+  if (!valid_dtype(dtype)) return fail(WF_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (M < 0 || d_model < 1 || n_out < 1) return fail(WF_ERR_INVALID_ARGUMENT, "bad sizes (M=%lld, d_model=%d, n_out=%d)",
+                                                     (long long)M, d_model, n_out);
+  if (M > kI32Max) return fail(WF_ERR_UNSUPPORTED, "M=%lld rows exceed 2^31", (long long)M);
+  if (group < 1 || group > 32 || (group & (group - 1)) || n_out % group)
+    return fail(WF_ERR_INVALID_ARGUMENT, "group must be a power of two <= 32 dividing n_out, got %d", group);
+  if (n_out > 256 || (n_out <= 32 ? 32 % n_out != 0 : n_out % 32 != 0))
+    return fail(WF_ERR_UNSUPPORTED, "n_out=%d: supported are divisors of 32 and multiples of 32 up to 256", n_out);
+  if (x_row_stride < d_model || out_row_stride < n_out)
+    return fail(WF_ERR_INVALID_ARGUMENT, "row strides must cover the rows");
+  if (M == 0) return ok();
+  if (!x || !w || !out) return fail(WF_ERR_INVALID_ARGUMENT, "null pointer argument");
+  const int rc = wf::launch_address_projection(x, dtype, M, d_model, x_row_stride, w, bias, n_out, group, normalize,
+                                               out, out_row_stride, status, static_cast<cudaStream_t>(stream));
+  if (rc) return cuda_fail(rc, "wf_address_projection");
+  return ok();
+}
+
 }  // extern "C"

@@ -73,4 +73,9 @@ size_t topk_smem_bytes(int R, int K);
 int topk_max_k();
 int attn_max_k();
 
+// Fused address projection (wf_addr_proj.cu): out[m, :] = normalize_group(x[m] W^T + b).
+int launch_address_projection(const void* x, int dtype, int64_t M, int K, int64_t x_stride, const void* w,
+                              const void* bias, int N, int group, int normalize, void* out, int64_t out_stride,
+                              int32_t* status, cudaStream_t stream);
+
 }  // namespace wf
