@@ -229,6 +229,29 @@ WF_API int wf_address_projection(const void* x, int32_t dtype, int64_t M, int32_
                                  const void* w, const void* bias, int32_t n_out, int32_t group, int32_t normalize,
                                  void* out, int64_t out_row_stride, int32_t* status, void* stream);
 
+/*
+ * Backward of wf_sparse_attention (the reference's fused path is forward-only; its
+ * non-fused training path gets these gradients from autograd through the gather,
+ * routing_attention/models/attention.py:35-56).  Given dout = dL/dout (B, H, Tq, D):
+ *   dq (B, H, Tq, D), dk and dv (B, H, Tk, D) = gradients of q, k, v; the indices
+ * carry no gradient.  Masked slots (flags & WF_ATTN_MASK_NEGATIVE) contribute
+ * nothing; duplicate indices add up.  Every dk/dv row is written (zeros for keys
+ * no query retrieved).  grad_dtype: WF_DTYPE_F32 or the input dtype; accumulation
+ * is fp32 and each gradient element is rounded once.  D in {32, 64, 128}.
+ * workspace: wf_sparse_attention_backward_workspace_bytes(B, H, Tq, Tk, K) bytes,
+ * 256-byte aligned (softmax probabilities and scaled ds per slot and head, and the
+ * key -> (query, slot) inverse index).
+ */
+WF_API size_t wf_sparse_attention_backward_workspace_bytes(int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t K);
+WF_API int wf_sparse_attention_backward(const void* q, const void* k, const void* v, int32_t dtype,
+                                        const int32_t* idx, int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t D,
+                                        int32_t K, const int64_t* q_strides, const int64_t* k_strides,
+                                        const int64_t* v_strides, const int64_t* idx_strides, const void* dout,
+                                        const int64_t* dout_strides, float scale, int32_t flags, void* dq, void* dk,
+                                        void* dv, int32_t grad_dtype, const int64_t* dq_strides,
+                                        const int64_t* dk_strides, const int64_t* dv_strides, void* workspace,
+                                        size_t workspace_bytes, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

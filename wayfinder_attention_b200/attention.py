@@ -16,10 +16,11 @@ Differences from the reference module, all deliberate:
     ``use_fused_sparse=False`` the addresses are first rounded to
     ``retrieval_config.dtype`` (fp16 by default), reproducing the non-fused
     path's retrieval numerics (``retrieval/index.py:188-207``);
-  * the sparse attention is forward-only (the reference's fused path is
-    ``@torch.no_grad`` too, ``kernels/fused_sparse.py:327``).  Attention-
-    probability dropout of the non-fused path is not implemented: calling it
-    in training mode with ``dropout > 0`` raises ``NotImplementedError``.
+  * the fused path is forward-only like the reference's (``@torch.no_grad``,
+    ``kernels/fused_sparse.py:327``); the non-fused path trains: its sparse
+    attention has a CUDA backward for q, k and v.  Attention-probability
+    dropout of the non-fused path is not implemented: calling it in training
+    mode with ``dropout > 0`` raises ``NotImplementedError``.
 """
 
 from __future__ import annotations

@@ -450,4 +450,57 @@ int wf_address_projection(const void* x, int32_t dtype, int64_t M, int32_t d_mod
   return ok();
 }
 
+
+size_t wf_sparse_attention_backward_workspace_bytes(int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t K) {
+  if (B <= 0 || H <= 0 || Tq <= 0 || Tk <= 0 || K <= 0) return 0;
+  return wf::attn_bwd_workspace_bytes(B, H, Tq, Tk, K);
+}
+
+int wf_sparse_attention_backward(const void* q, const void* k, const void* v, int32_t dtype, const int32_t* idx,
+                                 int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t D, int32_t K,
+                                 const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                                 const int64_t* idx_strides, const void* dout, const int64_t* dout_strides, float scale,
+                                 int32_t flags, void* dq, void* dk, void* dv, int32_t grad_dtype,
+                                 const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+                                 void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  int rc = check_attn(q, k, v, dtype, idx, B, H, Tq, Tk, D, K, q_strides, k_strides, v_strides, idx_strides, scale,
+                      flags, dq, grad_dtype, dq_strides);
+  if (rc) return rc;
+  if (B == 0 || H == 0 || (Tq == 0 && Tk == 0)) return ok();
+  if (D != 32 && D != 64 && D != 128) return fail(WF_ERR_UNSUPPORTED, "backward: head_dim D=%d not supported (32, 64, 128)", D);
+  if (grad_dtype != WF_DTYPE_F32 && grad_dtype != dtype)
+    return fail(WF_ERR_UNSUPPORTED, "backward: gradients are produced in fp32 or in the input dtype");
+  if (Tq * (int64_t)K > kI32Max || Tq >= (int64_t(1) << 22))
+    return fail(WF_ERR_UNSUPPORTED, "backward: Tq*K must be below 2^31 and Tq below 2^22");
+  const int esz = dtype_size(dtype), gsz = dtype_size(grad_dtype);
+  if ((rc = check_attn_tensor("dout", dout, dout_strides, esz))) return rc;
+  if (!dk || !dv || !dk_strides || !dv_strides) return fail(WF_ERR_INVALID_ARGUMENT, "dk/dv: null pointer");
+  if (dk_strides[3] != 1 || dv_strides[3] != 1) return fail(WF_ERR_INVALID_ARGUMENT, "dk/dv: last dimension must be contiguous");
+  auto vec_ok = [&](const void* ptr, const int64_t* s) {
+    return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && (s[0] * gsz) % 16 == 0 && (s[1] * gsz) % 16 == 0 &&
+           (s[2] * gsz) % 16 == 0;
+  };
+  wf::AttnBwdParams p{};
+  p.q = q; p.k = k; p.v = v; p.dout = dout; p.idx = idx; p.dq = dq; p.dk = dk; p.dv = dv;
+  p.qsb = q_strides[0]; p.qsh = q_strides[1]; p.qst = q_strides[2];
+  p.ksb = k_strides[0]; p.ksh = k_strides[1]; p.kst = k_strides[2];
+  p.vsb = v_strides[0]; p.vsh = v_strides[1]; p.vst = v_strides[2];
+  p.osb = dout_strides[0]; p.osh = dout_strides[1]; p.ost = dout_strides[2];
+  p.dqsb = dq_strides[0]; p.dqsh = dq_strides[1]; p.dqst = dq_strides[2];
+  p.dksb = dk_strides[0]; p.dksh = dk_strides[1]; p.dkst = dk_strides[2];
+  p.dvsb = dv_strides[0]; p.dvsh = dv_strides[1]; p.dvst = dv_strides[2];
+  p.isb = idx_strides[0]; p.ist = idx_strides[1]; p.iss = idx_strides[2];
+  p.B = (int)B; p.H = (int)H; p.Tq = (int)Tq; p.Tk = (int)Tk; p.D = D; p.K = K;
+  p.scale = scale;
+  p.mask_negative = (flags & WF_ATTN_MASK_NEGATIVE) ? 1 : 0;
+  p.dq_vec_ok = vec_ok(dq, dq_strides);
+  p.dk_vec_ok = vec_ok(dk, dk_strides);
+  p.dv_vec_ok = vec_ok(dv, dv_strides);
+  p.status = status;
+  rc = wf::launch_sparse_attention_backward(p, workspace, workspace_bytes, dtype, grad_dtype,
+                                            static_cast<cudaStream_t>(stream));
+  if (rc) return cuda_fail(rc, "wf_sparse_attention_backward");
+  return ok();
+}
+
 }  // extern "C"

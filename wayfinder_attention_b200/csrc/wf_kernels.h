@@ -78,4 +78,32 @@ int launch_address_projection(const void* x, int dtype, int64_t M, int K, int64_
                               const void* bias, int N, int group, int normalize, void* out, int64_t out_stride,
                               int32_t* status, cudaStream_t stream);
 
+// Backward of the sparse attention (wf_attn_bwd.cu).
+struct AttnBwdParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* dout;
+  const int32_t* idx;
+  void* dq;
+  void* dk;
+  void* dv;
+  int64_t qsb, qsh, qst, ksb, ksh, kst, vsb, vsh, vst, osb, osh, ost;
+  int64_t dqsb, dqsh, dqst, dksb, dksh, dkst, dvsb, dvsh, dvst;
+  int64_t isb, ist, iss;
+  int B, H, Tq, Tk, D, K;
+  float scale;
+  int mask_negative;
+  int dq_vec_ok, dk_vec_ok, dv_vec_ok;
+  float* P;      // [B][Tq][K][H] softmax probabilities (workspace)
+  float* DS;     // [B][Tq][K][H] scale * ds (workspace)
+  int32_t* cnt;  // [B][Tk] per-key counts, then fill cursors (workspace)
+  int32_t* off;  // [B][Tk + 1] list offsets (workspace)
+  int32_t* list; // [B][Tq * K] (t * K + slot) entries grouped by key (workspace)
+  int32_t* status;
+};
+size_t attn_bwd_workspace_bytes(int64_t B, int64_t H, int64_t Tq, int64_t Tk, int K);
+int launch_sparse_attention_backward(AttnBwdParams p, void* ws, size_t ws_bytes, int dtype, int grad_dtype,
+                                     cudaStream_t stream);
+
 }  // namespace wf

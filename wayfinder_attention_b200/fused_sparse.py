@@ -97,7 +97,51 @@ def _launch_attention(
     return out
 
 
-@torch.no_grad()
+def _launch_attention_backward(q, k, v, indices, dout, scale, mask_negative, status=None):
+    """(dq, dk, dv) of the sparse attention via ``wf_sparse_attention_backward``."""
+    dev = _lib.require_cuda(q, k, v, indices, dout)
+    lib = _lib.load_library()
+    B, H, Tq, D = q.shape
+    Tk = k.shape[2]
+    K = indices.shape[-1]
+    q, k, v = _attn_operand(q), _attn_operand(k), _attn_operand(v)
+    dout = _attn_operand(dout.to(q.dtype))
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    n = lib.wf_sparse_attention_backward_workspace_bytes(B, H, Tq, Tk, K)
+    ws = torch.empty(max(n, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.wf_sparse_attention_backward(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.dtype_code(q.dtype), indices.data_ptr(),
+            B, H, Tq, Tk, D, K, _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(indices),
+            dout.data_ptr(), _lib.strides(dout), float(scale), _lib.WF_ATTN_MASK_NEGATIVE if mask_negative else 0,
+            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _lib.dtype_code(q.dtype), _lib.strides(dq),
+            _lib.strides(dk), _lib.strides(dv), ws.data_ptr(), ws.numel(),
+            status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
+        )
+    _lib.check(rc)
+    return dq, dk, dv
+
+
+class _SparseMeatFunction(torch.autograd.Function):
+    """Sparse attention with a backward (``wf_sparse_attention_backward``); indices get no gradient."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, indices, scale, mask_negative, out_dtype):
+        out = _launch_attention(q, k, v, indices, scale, mask_negative=mask_negative, out_dtype=out_dtype)
+        ctx.save_for_backward(q, k, v, indices)
+        ctx.scale = scale
+        ctx.mask_negative = mask_negative
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, indices = ctx.saved_tensors
+        dq, dk, dv = _launch_attention_backward(q, k, v, indices, dout, ctx.scale, ctx.mask_negative)
+        return dq, dk, dv, None, None, None, None
+
+
 def sparse_meat_attention(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -117,7 +161,9 @@ def sparse_meat_attention(
     like ``fused_sparse.py:297-298``).  Returns (B, H, T, D) in ``q.dtype``
     unless ``out_dtype`` is given.  Negative indices wrap by Tk like torch
     indexing unless ``mask_negative`` is set, in which case they are excluded
-    from the softmax.
+    from the softmax.  Differentiable in q, k and v when autograd records (the
+    reference's gather path is too, ``fused_sparse.py:64-94``); the indices carry
+    no gradient.
     """
     del method, config
     _check_meat_shapes(q, k, v)
@@ -125,8 +171,13 @@ def sparse_meat_attention(
         q, k, v = q.float(), k.float(), v.float()
     if indices.dtype != torch.int32:
         indices = indices.to(torch.int32)
-    return _launch_attention(q, k, v, indices, scale, mask_negative=mask_negative, out_dtype=out_dtype,
-                             status=status)
+    if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
+        if status is not None:
+            raise ValueError("status is not supported on the differentiable path")
+        return _SparseMeatFunction.apply(q, k, v, indices, scale, mask_negative, out_dtype)
+    with torch.no_grad():
+        return _launch_attention(q, k, v, indices, scale, mask_negative=mask_negative, out_dtype=out_dtype,
+                                 status=status)
 
 
 def sparse_meat_attention_reference(q, k, v, indices, scale):
