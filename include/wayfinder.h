@@ -230,6 +230,25 @@ WF_API int wf_address_projection(const void* x, int32_t dtype, int64_t M, int32_
                                  void* out, int64_t out_row_stride, int32_t* status, void* stream);
 
 /*
+ * Causal top-K that retrieves only keys a padding mask keeps.  The reference's
+ * sparse path accepts attn_mask (a (B, T) key-padding mask, `input_ids != pad`,
+ * routing_attention/models/transformer.py:269-284) and ignores it
+ * (models/attention.py:456-490); here query t retrieves the K best keys j <= t with
+ * key_mask[b, j] != 0.  Slots a row cannot fill are -1 (masked pads; give
+ * WF_ATTN_MASK_NEGATIVE to the attention).  Queries and keys are the same T
+ * positions.  key_mask: (B, T) uint8, element strides mask_strides[2].  workspace:
+ * wf_causal_topk_key_mask_workspace_bytes(...) bytes, 256-byte aligned (the
+ * compacted key addresses, prefix counts and the position map, then the top-K
+ * workspace).  Other arguments as wf_causal_topk.
+ */
+WF_API size_t wf_causal_topk_key_mask_workspace_bytes(int64_t B, int64_t T, int32_t R, int32_t top_k, int32_t dtype);
+WF_API int wf_causal_topk_key_mask(const void* q_addr, const void* k_addr, int32_t dtype, int64_t B, int64_t T,
+                                   int32_t R, const int64_t* q_strides, const int64_t* k_strides,
+                                   const uint8_t* key_mask, const int64_t* mask_strides, int32_t top_k,
+                                   int32_t* idx_out, void* workspace, size_t workspace_bytes, int32_t* status,
+                                   void* stream);
+
+/*
  * Backward of wf_sparse_attention (the reference's fused path is forward-only; its
  * non-fused training path gets these gradients from autograd through the gather,
  * routing_attention/models/attention.py:35-56).  Given dout = dL/dout (B, H, Tq, D):

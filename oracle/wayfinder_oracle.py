@@ -101,6 +101,33 @@ def causal_topk(q: np.ndarray, k: np.ndarray, top_k: int, *, pad_mode: str = "re
     return out
 
 
+def causal_topk_key_mask(q: np.ndarray, k: np.ndarray, top_k: int, key_mask: np.ndarray) -> np.ndarray:
+    """Causal top-K over the keys a (B, T) padding mask keeps; unfilled slots are -1.
+
+    The reference's sparse path ignores its attn_mask (models/attention.py:456-490);
+    the semantics here are those of its dense path, which drops masked keys
+    (attention.py:157-167, mask built as input_ids != pad at transformer.py:269-270):
+    query t ranks keys j <= t with key_mask[b, j] != 0 by fp32 score, ties to the
+    lower index.  Small cases only (a Python loop over rows).
+    """
+    q = np.asarray(q, dtype=np.float32)
+    k = np.asarray(k, dtype=np.float32)
+    B, T, _ = q.shape
+    K = min(int(top_k), T)
+    out = np.full((B, T, K), -1, dtype=np.int32)
+    for b in range(B):
+        valid = np.nonzero(np.asarray(key_mask[b]) != 0)[0]
+        for t in range(T):
+            cand = valid[valid <= t]
+            if cand.size == 0:
+                continue
+            sc = (k[b, cand] @ q[b, t]).astype(np.float32)
+            order = np.lexsort((cand, -sc.astype(np.float64)))
+            sel = cand[order][:K]
+            out[b, t, : sel.size] = sel
+    return out
+
+
 def sparse_meat_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, idx: np.ndarray, scale: float, *,
                           mask_negative: bool = False, rows: np.ndarray | None = None,
                           chunk: int = 256) -> np.ndarray:

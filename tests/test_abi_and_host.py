@@ -101,6 +101,19 @@ def test_address_projection_entry_validates_before_launch():
     assert lib.wf_address_projection(None, 0, 0, 256, 256, None, None, 64, 32, 1, None, 64, None, None) == _lib.WF_OK
 
 
+def test_key_mask_entry_validates_before_launch():
+    lib = _lib.load_library()
+    p = ctypes.c_void_p(4096)
+    s = _i64(4096, 32, 1)
+    ms = _i64(128, 1)
+    n = lib.wf_causal_topk_key_mask_workspace_bytes(1, 128, 32, 16, 0)
+    assert n > 0
+    rc = lib.wf_causal_topk_key_mask(p, p, 0, 1, 128, 32, s, s, None, ms, 16, p, p, n, None, None)
+    assert rc == _lib.WF_ERR_INVALID_ARGUMENT and b"key_mask" in lib.wf_last_error()
+    rc = lib.wf_causal_topk_key_mask(p, p, 0, 1, 128, 32, s, s, p, ms, 16, p, p, n - 1, None, None)
+    assert rc == _lib.WF_ERR_INVALID_ARGUMENT and b"workspace" in lib.wf_last_error()
+
+
 def test_python_api_validates_like_reference():
     a = torch.zeros(1, 8, 32)
     with pytest.raises(ValueError, match="shape mismatch"):

@@ -44,6 +44,8 @@ EXPORTED_SYMBOLS = (
     "wf_address_projection",
     "wf_sparse_attention_backward",
     "wf_sparse_attention_backward_workspace_bytes",
+    "wf_causal_topk_key_mask",
+    "wf_causal_topk_key_mask_workspace_bytes",
 )
 
 _DTYPE_CODES = {
@@ -109,6 +111,12 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.wf_sparse_attention_backward.argtypes = [
         _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i32, _i32, _i64p, _i64p, _i64p, _i64p,
         _vp, _i64p, _f32, _i32, _vp, _vp, _vp, _i32, _i64p, _i64p, _i64p, _vp, ctypes.c_size_t, _vp, _vp,
+    ]
+    lib.wf_causal_topk_key_mask_workspace_bytes.restype = ctypes.c_size_t
+    lib.wf_causal_topk_key_mask_workspace_bytes.argtypes = [_i64, _i64, _i32, _i32, _i32]
+    lib.wf_causal_topk_key_mask.restype = ctypes.c_int
+    lib.wf_causal_topk_key_mask.argtypes = [
+        _vp, _vp, _i32, _i64, _i64, _i32, _i64p, _i64p, _vp, _i64p, _i32, _vp, _vp, ctypes.c_size_t, _vp, _vp,
     ]
 
 

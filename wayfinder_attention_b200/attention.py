@@ -142,6 +142,7 @@ class LearnedAddressSparseAttention(nn.Module):
         address_module: LearnedAddressModule | None = None,
         retrieval_config: RetrievalConfig | dict | None = None,
         pad_mode: str = "reference",
+        mask_padded_keys: bool = False,
     ):
         super().__init__()
         assert d_model % n_heads == 0
@@ -150,6 +151,9 @@ class LearnedAddressSparseAttention(nn.Module):
         self.scale = self.head_dim ** -0.5
         self.top_k = top_k
         self.pad_mode = pad_mode
+        # Honour attn_mask (B, T) as a key-padding mask on the fused path; the
+        # reference ignores it there, so the default keeps its behaviour.
+        self.mask_padded_keys = mask_padded_keys
         self._retrieval_cfg = _resolve_retrieval_cfg(retrieval_config, top_k)
         self.q_proj = nn.Linear(d_model, d_model)
         self.k_proj = nn.Linear(d_model, d_model)
@@ -170,15 +174,17 @@ class LearnedAddressSparseAttention(nn.Module):
         return_attention: bool = False,
         **kwargs,
     ):
-        # attn_mask is accepted and ignored, as on the reference's sparse path (attention.py:456-490).
+        # attn_mask is ignored, as on the reference's sparse path (attention.py:456-490), unless the
+        # module was built with mask_padded_keys=True (fused path: padded keys are never retrieved).
         B, T, D = x.shape
         q = self.q_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
         k = self.k_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
         v = self.v_proj(x).view(B, T, self.n_heads, self.head_dim).transpose(1, 2)
         q_addr, k_addr = self.address.forward_query_key(x)
         if self._retrieval_cfg.use_fused_sparse:
+            key_mask = attn_mask if (self.mask_padded_keys and attn_mask is not None and not bool(attn_mask.all())) else None
             meat, candidate_idx = fused_sparse_attention(
-                q_addr, k_addr, q, k, v, self.top_k, self.scale, pad_mode=self.pad_mode
+                q_addr, k_addr, q, k, v, self.top_k, self.scale, pad_mode=self.pad_mode, key_mask=key_mask
             )
         else:
             if self.training and self.dropout.p > 0:

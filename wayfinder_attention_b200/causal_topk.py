@@ -103,11 +103,14 @@ def causal_topk(
     prefer_triton: bool = False,
     pad_mode: str = "reference",
     status: torch.Tensor | None = None,
+    key_mask: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Causal top-K retrieval: (B, T, R) x (B, T, R) -> (B, T, min(top_k, T)) int32.
 
     Mirrors ``causal_topk`` (``routing_attention/kernels/causal_topk.py:470-521``),
     including its ``ValueError`` messages for mismatched or non-3-D inputs.
+    ``key_mask`` (B, T), an extension: only keys with a nonzero mask are retrieved,
+    and slots a row cannot fill are -1 (masked pads) whatever ``pad_mode`` says.
     """
     del method, prefer_triton  # one exact backend
     if query.shape != key.shape:
@@ -120,7 +123,32 @@ def causal_topk(
         return torch.zeros(B, T, 0, dtype=torch.int32, device=query.device)
     _lib.require_cuda(query, key)
     q, k, _ = promote_compute_dtype(query, key, dtype)
+    if key_mask is not None:
+        return _launch_topk_key_mask(q, k, top_k, key_mask, status=status)
     return _launch_topk(q, k, top_k, pad_mode, status=status)
+
+
+def _launch_topk_key_mask(q: torch.Tensor, k: torch.Tensor, top_k: int, key_mask: torch.Tensor,
+                          status: torch.Tensor | None = None) -> torch.Tensor:
+    """``wf_causal_topk_key_mask``: top-K over the keys ``key_mask`` (B, T) keeps."""
+    dev = _lib.require_cuda(q, k, key_mask)
+    lib = _lib.load_library()
+    B, T, R = q.shape
+    if tuple(key_mask.shape) != (B, T):
+        raise ValueError(f"key_mask must have shape {(B, T)}, got {tuple(key_mask.shape)}")
+    m = key_mask.to(torch.uint8)
+    k_eff = min(int(top_k), T)
+    out = torch.empty(B, T, k_eff, dtype=torch.int32, device=dev)
+    n = lib.wf_causal_topk_key_mask_workspace_bytes(B, T, R, int(top_k), _lib.dtype_code(q.dtype))
+    ws = torch.empty(max(n, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.wf_causal_topk_key_mask(
+            q.data_ptr(), k.data_ptr(), _lib.dtype_code(q.dtype), B, T, R, _lib.strides(q), _lib.strides(k),
+            m.data_ptr(), _lib.strides(m), int(top_k), out.data_ptr(), ws.data_ptr(), ws.numel(),
+            status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
+        )
+    _lib.check(rc)
+    return out
 
 
 def causal_topk_reference(query: torch.Tensor, key: torch.Tensor, top_k: int) -> torch.Tensor:

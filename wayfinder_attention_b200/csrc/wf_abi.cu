@@ -503,4 +503,44 @@ int wf_sparse_attention_backward(const void* q, const void* k, const void* v, in
   return ok();
 }
 
+
+size_t wf_causal_topk_key_mask_workspace_bytes(int64_t B, int64_t T, int32_t R, int32_t top_k, int32_t dtype) {
+  if (B <= 0 || T <= 0 || top_k <= 0 || R < 1 || !valid_dtype(dtype)) return 0;
+  const size_t inner = (wf_causal_topk_workspace_bytes(B, T, T, R, top_k, dtype) + 255) / 256 * 256;
+  return wf::topk_key_mask_prep_bytes(B, T, R, dtype_size(dtype)) + inner;
+}
+
+int wf_causal_topk_key_mask(const void* q_addr, const void* k_addr, int32_t dtype, int64_t B, int64_t T, int32_t R,
+                            const int64_t* q_strides, const int64_t* k_strides, const uint8_t* key_mask,
+                            const int64_t* mask_strides, int32_t top_k, int32_t* idx_out, void* workspace,
+                            size_t workspace_bytes, int32_t* status, void* stream) {
+  int32_t k_eff = 0, rt = 0, rs = 1, r0 = 0;
+  int rc = check_topk(q_addr, k_addr, dtype, B, T, T, R, q_strides, k_strides, top_k, WF_PAD_MASKED, rt, rs, r0,
+                      idx_out, &k_eff);
+  if (rc) return rc;
+  if (k_eff == 0 || B == 0 || T == 0) return ok();
+  if (!key_mask || !mask_strides) return fail(WF_ERR_INVALID_ARGUMENT, "key_mask: null pointer");
+  const size_t need = wf_causal_topk_key_mask_workspace_bytes(B, T, R, top_k, dtype);
+  if (!workspace || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(WF_ERR_INVALID_ARGUMENT, "wf_causal_topk_key_mask: workspace missing, not 256-byte aligned or "
+                "smaller than %zu bytes (wf_causal_topk_key_mask_workspace_bytes)", need);
+  const size_t prep = wf::topk_key_mask_prep_bytes(B, T, R, dtype_size(dtype));
+  wf::TopkParams p{};
+  p.q = q_addr;
+  p.k = k_addr;
+  p.qsb = q_strides[0]; p.qst = q_strides[1]; p.qsr = q_strides[2];
+  p.ksb = k_strides[0]; p.kst = k_strides[1]; p.ksr = k_strides[2];
+  p.B = (int)B; p.Tq = (int)T; p.Tk = (int)T; p.R = R; p.K = k_eff;
+  p.pad_mode = WF_PAD_MASKED;
+  p.rt = rt; p.rs = rs; p.r0 = r0;
+  p.idx = idx_out;
+  p.status = status;
+  p.ws = static_cast<unsigned char*>(workspace) + prep;
+  p.ws_bytes = workspace_bytes - prep;
+  rc = wf::launch_topk_key_mask(p, dtype, key_mask, mask_strides[0], mask_strides[1], workspace,
+                                static_cast<cudaStream_t>(stream));
+  if (rc) return cuda_fail(rc, "wf_causal_topk_key_mask");
+  return ok();
+}
+
 }  // extern "C"

@@ -25,6 +25,9 @@ struct TopkParams {
   int32_t* status;       // nullable; bit 1 set if a bounded wait timed out
   void* ws;              // workspace of the tensor-core kernel (see topk_tc_workspace_bytes)
   size_t ws_bytes;
+  // Optional [B][Tq] per-row key limits (replaces the row map): row l of batch b may
+  // retrieve keys j < lim[b][l]; non-decreasing along the rows.  Null: causal row map.
+  const int32_t* lim;
 };
 
 // Sparse attention over retrieved rows, indices shared across heads.
@@ -77,6 +80,12 @@ int attn_max_k();
 int launch_address_projection(const void* x, int dtype, int64_t M, int K, int64_t x_stride, const void* w,
                               const void* bias, int N, int group, int normalize, void* out, int64_t out_stride,
                               int32_t* status, cudaStream_t stream);
+
+// Top-K over the keys a (B, T) padding mask keeps (wf_keymask.cu).  `prep` holds
+// topk_key_mask_prep_bytes; p.ws the top-K workspace for (B, T, T).
+size_t topk_key_mask_prep_bytes(int64_t B, int64_t T, int R, int esz);
+int launch_topk_key_mask(TopkParams p, int dtype, const uint8_t* mask, int64_t msb, int64_t mst, void* prep,
+                         cudaStream_t stream);
 
 // Backward of the sparse attention (wf_attn_bwd.cu).
 struct AttnBwdParams {

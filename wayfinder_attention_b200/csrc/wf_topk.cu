@@ -57,8 +57,9 @@ __global__ void __launch_bounds__(kThreads, 1) causal_topk_kernel(const TopkPara
   const int b = blockIdx.y;
   const int l0 = tile * kRows;
   const int nrows = min(kRows, p.Tq - l0);
-  const int g0 = ((l0 / p.rt) * p.rs + p.r0) * p.rt + (l0 % p.rt);
-  const int key_end = min(g0 + nrows, p.Tk);
+  const int g0 = p.lim ? 0 : ((l0 / p.rt) * p.rs + p.r0) * p.rt + (l0 % p.rt);
+  const int32_t* lrow = p.lim ? p.lim + (int64_t)b * p.Tq + l0 : nullptr;  // per-row key limits
+  const int key_end = min(lrow ? lrow[nrows - 1] : g0 + nrows, p.Tk);
 
   const TI* qb = reinterpret_cast<const TI*>(p.q) + (int64_t)b * p.qsb;
   const TI* kb = reinterpret_cast<const TI*>(p.k) + (int64_t)b * p.ksb;
@@ -112,7 +113,7 @@ __global__ void __launch_bounds__(kThreads, 1) causal_topk_kernel(const TopkPara
     for (int rr = 0; rr < kRows / 8; ++rr) {
       const int r = warp * (kRows / 8) + rr;
       if (r >= nrows) break;
-      const int g = g0 + r;
+      const int g = lrow ? lrow[r] - 1 : g0 + r;
       if (c0 > g) continue;
       uint32_t* bk = bkey + r * CAP;
       int* bi = bidx + r * CAP;
@@ -154,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1) causal_topk_kernel(const TopkPara
   for (int rr = 0; rr < kRows / 8; ++rr) {
     const int r = warp * (kRows / 8) + rr;
     if (r >= nrows) break;
-    const int g = g0 + r;
+    const int g = lrow ? lrow[r] - 1 : g0 + r;
     uint32_t* bk = bkey + r * CAP;
     int* bi = bidx + r * CAP;
     int n = cnt[r];

@@ -98,6 +98,7 @@ struct TcParams {
   int32_t* status;
   uint64_t* ws;      // [B*Tq][kLists][KW] candidate composites (key << 32 | ~index)
   int32_t* ws_cnt;   // [B*Tq][kLists] candidate counts
+  const int32_t* lim;  // optional [B][Tq] per-row key limits (see TopkParams)
 };
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -206,8 +207,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b = blockIdx.y;
   const int l0 = tile * kM;
   const int nrows = min(kM, p.Tq - l0);
-  const int g0 = ((l0 / p.rt) * p.rs + p.r0) * p.rt + (l0 % p.rt);
-  const int key_end = min(g0 + nrows, p.Tk);
+  const int g0 = p.lim ? 0 : ((l0 / p.rt) * p.rs + p.r0) * p.rt + (l0 % p.rt);
+  const int32_t* lrow = p.lim ? p.lim + (int64_t)b * p.Tq + l0 : nullptr;  // per-row key limits
+  const int key_end = min(lrow ? lrow[nrows - 1] : g0 + nrows, p.Tk);
   const int nchunks = (key_end + kN - 1) / kN;
   const int n_own = nchunks > (int)rank ? (nchunks - (int)rank + 1) / 2 : 0;
   const int n_work = (WF_TOPK_SKIP & 2) ? n_own : 2 * n_own;  // pass 1 + pass 2 items
@@ -306,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qd = warp & 3, hf = warp >> 2;
     const int r = 32 * qd + lane;  // query row in the tile = TMEM lane
     const bool row_ok = r < nrows;
-    const int g = g0 + r;
+    const int g = lrow ? (row_ok ? lrow[r] - 1 : -1) : g0 + r;
     const uint32_t lane_base = (uint32_t)(32 * qd) << 16;
     const int pair_bar = 1 + qd;   // named barrier of the two warps of this quadrant
     float qabs = 0.f;
@@ -636,6 +638,7 @@ struct FinParams {
   int B, Tq, Tk, K, cap;
   int pad_mode;
   int rt, rs, r0;
+  const int32_t* lim;
 };
 
 constexpr int kFinWarps = 8;
@@ -644,7 +647,7 @@ template <int EPLF, int SE>
 __device__ __forceinline__ void finalize_row(const FinParams& p, int64_t row, const int (&nl)[kLists], int lane,
                                              uint32_t* bk, int* bi) {
   const int l = (int)(row % p.Tq);
-  const int g = ((l / p.rt) * p.rs + p.r0) * p.rt + (l % p.rt);
+  const int g = p.lim ? p.lim[row] - 1 : ((l / p.rt) * p.rs + p.r0) * p.rt + (l % p.rt);
   const int e1 = nl[0], e2 = e1 + nl[1], e3 = e2 + nl[2], n = e3 + nl[3];
   const uint64_t* a = p.ws + row * kLists * p.cap;
   // The row's concatenated lists are consumed in blocks of up to 32*EPLF entries
@@ -835,6 +838,7 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
     t.B = nb; t.Tq = p.Tq; t.Tk = p.Tk; t.K = p.K;
     t.pad_mode = p.pad_mode;
     t.rt = p.rt; t.rs = p.rs; t.r0 = p.r0;
+    t.lim = p.lim ? p.lim + (size_t)b0 * p.Tq : nullptr;
     t.idx = p.idx + (size_t)b0 * p.Tq * p.K;
     t.status = p.status;
     t.ws = ws;
@@ -861,6 +865,7 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
     f.B = nb; f.Tq = p.Tq; f.Tk = p.Tk; f.K = p.K; f.cap = KW;
     f.pad_mode = p.pad_mode;
     f.rt = p.rt; f.rs = p.rs; f.r0 = p.r0;
+    f.lim = t.lim;
     const size_t rows = (size_t)nb * p.Tq;
     topk_finalize_kernel<SE, KW - 128><<<(unsigned)((rows + kFinWarps - 1) / kFinWarps), kFinWarps * 32, 0, stream>>>(f);
     e = cudaGetLastError();

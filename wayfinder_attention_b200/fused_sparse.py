@@ -201,12 +201,15 @@ def fused_sparse_attention(
     pad_mode: str = "reference",
     out_dtype: torch.dtype | None = None,
     status: torch.Tensor | None = None,
+    key_mask: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Causal top-K retrieval + sparse attention: returns (out (B,H,T,D), indices (B,T,K) int32).
 
     Mirrors ``fused_sparse_attention`` (``routing_attention/kernels/fused_sparse.py:327-356``).
     ``pad_mode="masked"`` excludes the pad slots of rows ``i < K-1`` from the
     softmax instead of attending to them as the reference does.
+    ``key_mask`` (B, T), an extension (the reference ignores padding here): padded
+    keys are never retrieved and unfilled slots are masked.
     """
     del retrieval_method, meat_method, meat_config
     if q_search.shape != k_search.shape:
@@ -232,6 +235,13 @@ def fused_sparse_attention(
     out = torch.empty(B, H, T, D, dtype=out_dtype or q.dtype, device=dev)
     if status is not None and (status.dtype != torch.int32 or not status.is_cuda):
         raise ValueError("status must be an int32 CUDA tensor")
+    if key_mask is not None:
+        # padded keys are never retrieved; slots a row cannot fill are masked out of the softmax
+        from .causal_topk import _launch_topk_key_mask
+
+        idx = _launch_topk_key_mask(qa, ka, int(top_k), key_mask, status=status)
+        out = _launch_attention(q, k, v, idx, scale, mask_negative=True, out_dtype=out_dtype, status=status)
+        return out, idx
     ws = _lib.workspace(B, T, T, R, int(top_k), qa.dtype, dev)
     with torch.cuda.device(dev):
         rc = lib.wf_fused_sparse_attention(
