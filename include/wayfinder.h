@@ -157,6 +157,22 @@ WF_API int wf_sparse_attention_cyclic_kv(const void* q, const void* k, const voi
                                          int32_t* status, void* stream);
 
 /*
+ * wf_sparse_attention with attention-probability dropout, for training.  The
+ * reference's training path applies nn.Dropout to the softmax probabilities before
+ * the weighted sum (routing_attention/models/attention.py:50-54); here probability
+ * (b, h, t, k) is kept with probability 1 - drop_rate and scaled by 1 / (1 - drop_rate),
+ * the keep decision being u >= drop_rate for u = a counter-based uniform of drop_seed
+ * and the element's flat index ((b*H + h)*Tq + t)*K + k (SplitMix64 output function,
+ * 24 bits; the backward recomputes the same mask).  drop_rate in [0, 1).
+ */
+WF_API int wf_sparse_attention_dropout(const void* q, const void* k, const void* v, int32_t dtype,
+                                       const int32_t* idx, int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t D,
+                                       int32_t K, const int64_t* q_strides, const int64_t* k_strides,
+                                       const int64_t* v_strides, const int64_t* idx_strides, float scale,
+                                       int32_t flags, float drop_rate, uint64_t drop_seed, void* out,
+                                       int32_t out_dtype, const int64_t* out_strides, int32_t* status, void* stream);
+
+/*
  * Retrieval + attention in one call.  Replaces fused_sparse_attention()
  * (routing_attention/kernels/fused_sparse.py:327-356): wf_causal_topk into idx_out,
  * then wf_sparse_attention over it (masking pads when pad_mode == WF_PAD_MASKED).
@@ -257,6 +273,7 @@ WF_API int wf_causal_topk_key_mask(const void* q_addr, const void* k_addr, int32
  * nothing; duplicate indices add up.  Every dk/dv row is written (zeros for keys
  * no query retrieved).  grad_dtype: WF_DTYPE_F32 or the input dtype; accumulation
  * is fp32 and each gradient element is rounded once.  D in {32, 64, 128}.
+ * drop_rate / drop_seed: those of the forward (wf_sparse_attention_dropout); 0 = none.
  * workspace: wf_sparse_attention_backward_workspace_bytes(B, H, Tq, Tk, K) bytes,
  * 256-byte aligned (softmax probabilities and scaled ds per slot and head, and the
  * key -> (query, slot) inverse index).
@@ -266,8 +283,8 @@ WF_API int wf_sparse_attention_backward(const void* q, const void* k, const void
                                         const int32_t* idx, int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t D,
                                         int32_t K, const int64_t* q_strides, const int64_t* k_strides,
                                         const int64_t* v_strides, const int64_t* idx_strides, const void* dout,
-                                        const int64_t* dout_strides, float scale, int32_t flags, void* dq, void* dk,
-                                        void* dv, int32_t grad_dtype, const int64_t* dq_strides,
+                                        const int64_t* dout_strides, float scale, int32_t flags, float drop_rate,
+                                        uint64_t drop_seed, void* dq, void* dk, void* dv, int32_t grad_dtype, const int64_t* dq_strides,
                                         const int64_t* dk_strides, const int64_t* dv_strides, void* workspace,
                                         size_t workspace_bytes, int32_t* status, void* stream);
 

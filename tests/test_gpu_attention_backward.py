@@ -121,3 +121,77 @@ def test_module_trains_through_the_sparse_path(cuda_device):
             assert gw is not None and torch.isfinite(gw).all() and gw.abs().sum() > 0, name
         opt.step()
     assert losses[-1] < losses[0]
+
+
+def _keep_mask(seed, B, H, T, K, rate):
+    """The kernels' keep decisions, recomputed in numpy (SplitMix64 output function of
+    seed + (idx + 1) * 0x9E3779B97F4A7C15, 24 high bits, keep when u >= rate)."""
+    import numpy as np
+
+    idx = np.arange(B * H * T * K, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        z = np.uint64(seed) + (idx + np.uint64(1)) * np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        z ^= z >> np.uint64(31)
+    u = (z >> np.uint64(40)).astype(np.float64) / 16777216.0
+    return torch.from_numpy((u >= float(np.float32(rate))).reshape(B, H, T, K))
+
+
+def _reference_dropout(q, k, v, idx, scale, dout, keep, rate):
+    q, k, v = (x.double().detach().requires_grad_(True) for x in (q, k, v))
+    Tk = k.shape[2]
+    ic = idx.long() % Tk
+    B = q.shape[0]
+    bidx = torch.arange(B, device=q.device)[:, None, None]
+    ksel = k.permute(0, 2, 1, 3)[bidx, ic]
+    vsel = v.permute(0, 2, 1, 3)[bidx, ic]
+    p = torch.softmax(torch.einsum("bhtd,btkhd->bhtk", q, ksel) * scale, dim=-1)
+    p = p * keep.to(p.device, p.dtype) / (1.0 - rate)
+    out = torch.einsum("bhtk,btkhd->bhtd", p, vsel)
+    out.backward(dout.double())
+    return out.detach(), q.grad, k.grad, v.grad
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_dropout_forward_and_backward_match_autograd(dtype, cuda_device):
+    from wayfinder_attention_b200 import sparse_meat_attention
+
+    B, H, T, D, K, rate, seed = 2, 4, 300, 64, 32, 0.25, 123456789
+    q, k, v, idx, dout = _case(B, H, T, T, D, K, dtype, "bthd", False, False, 77, cuda_device)
+    keep = _keep_mask(seed, B, H, T, K, rate)
+    assert abs(1.0 - keep.float().mean().item() - rate) < 0.01
+    qg, kg, vg = (x.detach().clone().requires_grad_(True) for x in (q, k, v))
+    out = sparse_meat_attention(qg, kg, vg, idx, D ** -0.5, dropout_p=rate, dropout_seed=seed)
+    out.backward(dout)
+    want_out, dq, dk, dv = _reference_dropout(q, k, v, idx, D ** -0.5, dout, keep, rate)
+    assert _close(out.detach(), want_out, dtype), "out"
+    assert _close(qg.grad, dq, dtype), "dq"
+    assert _close(kg.grad, dk, dtype), "dk"
+    assert _close(vg.grad, dv, dtype), "dv"
+    # the no-grad forward draws the same mask from the same seed
+    with torch.no_grad():
+        again = sparse_meat_attention(q, k, v, idx, D ** -0.5, dropout_p=rate, dropout_seed=seed)
+    assert torch.equal(again, out.detach())
+
+
+def test_module_trains_with_attention_dropout(cuda_device):
+    from wayfinder_attention_b200 import LearnedAddressSparseAttention
+
+    torch.manual_seed(12)
+    m = LearnedAddressSparseAttention(128, 2, top_k=16, dropout=0.1,
+                                      retrieval_config={"use_fused_sparse": False}).to(cuda_device).train()
+    x = torch.randn(2, 128, 128, device=cuda_device)
+    target = torch.randn(2, 128, 128, device=cuda_device)
+    opt = torch.optim.SGD(m.parameters(), lr=0.1)
+    losses = []
+    for _ in range(4):
+        opt.zero_grad()
+        loss = ((m(x) - target) ** 2).mean()
+        loss.backward()
+        losses.append(loss.item())
+        opt.step()
+    assert losses[-1] < losses[0]
+    m.eval()
+    with torch.no_grad():
+        assert torch.equal(m(x), m(x))  # no dropout in eval mode

@@ -46,6 +46,7 @@ EXPORTED_SYMBOLS = (
     "wf_sparse_attention_backward_workspace_bytes",
     "wf_causal_topk_key_mask",
     "wf_causal_topk_key_mask_workspace_bytes",
+    "wf_sparse_attention_dropout",
 )
 
 _DTYPE_CODES = {
@@ -110,7 +111,13 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.wf_sparse_attention_backward.restype = ctypes.c_int
     lib.wf_sparse_attention_backward.argtypes = [
         _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i32, _i32, _i64p, _i64p, _i64p, _i64p,
-        _vp, _i64p, _f32, _i32, _vp, _vp, _vp, _i32, _i64p, _i64p, _i64p, _vp, ctypes.c_size_t, _vp, _vp,
+        _vp, _i64p, _f32, _i32, _f32, ctypes.c_uint64, _vp, _vp, _vp, _i32, _i64p, _i64p, _i64p, _vp,
+        ctypes.c_size_t, _vp, _vp,
+    ]
+    lib.wf_sparse_attention_dropout.restype = ctypes.c_int
+    lib.wf_sparse_attention_dropout.argtypes = [
+        _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i32, _i32, _i64p, _i64p, _i64p, _i64p, _f32, _i32,
+        _f32, ctypes.c_uint64, _vp, _i32, _i64p, _vp, _vp,
     ]
     lib.wf_causal_topk_key_mask_workspace_bytes.restype = ctypes.c_size_t
     lib.wf_causal_topk_key_mask_workspace_bytes.argtypes = [_i64, _i64, _i32, _i32, _i32]

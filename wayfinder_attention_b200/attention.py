@@ -18,9 +18,9 @@ Differences from the reference module, all deliberate:
     path's retrieval numerics (``retrieval/index.py:188-207``);
   * the fused path is forward-only like the reference's (``@torch.no_grad``,
     ``kernels/fused_sparse.py:327``); the non-fused path trains: its sparse
-    attention has a CUDA backward for q, k and v.  Attention-probability
-    dropout of the non-fused path is not implemented: calling it in training
-    mode with ``dropout > 0`` raises ``NotImplementedError``.
+    attention has a CUDA backward for q, k and v and applies the module's
+    attention-probability dropout in training mode (its own counter-based
+    generator, so the masks differ from PyTorch's nn.Dropout draws).
 """
 
 from __future__ import annotations
@@ -187,15 +187,11 @@ class LearnedAddressSparseAttention(nn.Module):
                 q_addr, k_addr, q, k, v, self.top_k, self.scale, pad_mode=self.pad_mode, key_mask=key_mask
             )
         else:
-            if self.training and self.dropout.p > 0:
-                raise NotImplementedError(
-                    "attention-probability dropout of the non-fused path is not implemented "
-                    "(forward-only kernels); use eval() or retrieval_config.use_fused_sparse=True"
-                )
             rdt = _DTYPES.get(self._retrieval_cfg.dtype, torch.float16)
             candidate_idx = causal_topk(q_addr.to(rdt), k_addr.to(rdt), self.top_k, pad_mode=self.pad_mode)
             meat = sparse_meat_attention(
-                q, k, v, candidate_idx, self.scale, mask_negative=self.pad_mode == "masked"
+                q, k, v, candidate_idx, self.scale, mask_negative=self.pad_mode == "masked",
+                dropout_p=self.dropout.p if self.training else 0.0,
             )
         out = meat.transpose(1, 2).contiguous().view(B, T, D)
         out = self.out_proj(out)
@@ -265,17 +261,13 @@ class KeyVectorSparseAttention(nn.Module):
             meat, candidate_idx = fused_sparse_attention(qs, ks, q, k, v, self.top_k, self.scale,
                                                          pad_mode=self.pad_mode)
         else:
-            if self.training and self.dropout.p > 0:
-                raise NotImplementedError(
-                    "attention-probability dropout of the non-fused path is not implemented "
-                    "(forward-only kernels); use eval() or retrieval_config.use_fused_sparse=True"
-                )
             if self.use_fast_retrieval:
                 rdt = _DTYPES.get(self._retrieval_cfg.dtype, torch.float16)
                 qs, ks = qs.to(rdt), ks.to(rdt)
             candidate_idx = causal_topk(qs, ks, self.top_k, pad_mode=self.pad_mode)
             meat = sparse_meat_attention(q, k, v, candidate_idx, self.scale,
-                                         mask_negative=self.pad_mode == "masked")
+                                         mask_negative=self.pad_mode == "masked",
+                                         dropout_p=self.dropout.p if self.training else 0.0)
         out = self.out_proj(meat.transpose(1, 2).contiguous().view(B, T, D))
         if return_attention:
             k_eff = candidate_idx.shape[-1]
@@ -361,18 +353,14 @@ class RoutingSparseAttention(nn.Module):
             meat, candidate_idx = fused_sparse_attention(q_r, k_r, q, k, v, self.top_k, self.scale,
                                                          pad_mode=self.pad_mode)
         else:
-            if self.training and self.dropout.p > 0:
-                raise NotImplementedError(
-                    "attention-probability dropout of the non-fused path is not implemented "
-                    "(forward-only kernels); use eval() or retrieval_config.use_fused_sparse=True"
-                )
             if isinstance(self.router, MultiScaleRouter):
                 candidate_idx = self.router.retrieve_indices(x, self.top_k, self.layer_idx).to(torch.int32)
             else:
                 q_r, k_r = self._get_query_key_routing(x)
                 rdt = _DTYPES.get(self._retrieval_cfg.dtype, torch.float16)
                 candidate_idx = causal_topk(q_r.to(rdt), k_r.to(rdt), self.top_k, pad_mode=self.pad_mode)
-            meat = sparse_meat_attention(q, k, v, candidate_idx, self.scale, mask_negative=self.pad_mode == "masked")
+            meat = sparse_meat_attention(q, k, v, candidate_idx, self.scale, mask_negative=self.pad_mode == "masked",
+                                         dropout_p=self.dropout.p if self.training else 0.0)
         out = self.out_proj(meat.transpose(1, 2).contiguous().view(B, T, D))
         if return_attention:
             k_eff = candidate_idx.shape[-1]

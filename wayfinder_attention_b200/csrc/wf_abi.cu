@@ -176,7 +176,8 @@ int attention_impl(const void* q, const void* k, const void* v, int32_t dtype, c
                    int64_t H, int64_t Tq, int64_t Tk, int32_t D, int32_t K, const int64_t* q_strides,
                    const int64_t* k_strides, const int64_t* v_strides, const int64_t* idx_strides, float scale,
                    int32_t flags, void* out, int32_t out_dtype, const int64_t* out_strides, int32_t* status,
-                   void* stream, int32_t kv_tile, int32_t kv_world, int64_t k_rank_stride, int64_t v_rank_stride) {
+                   void* stream, int32_t kv_tile, int32_t kv_world, int64_t k_rank_stride, int64_t v_rank_stride,
+                   float drop_rate = 0.f, uint64_t drop_seed = 0) {
   int rc = check_attn(q, k, v, dtype, idx, B, H, Tq, Tk, D, K, q_strides, k_strides, v_strides, idx_strides,
                       scale, flags, out, out_dtype, out_strides);
   if (rc) return rc;
@@ -196,6 +197,8 @@ int attention_impl(const void* q, const void* k, const void* v, int32_t dtype, c
   p.kv_world = kv_world;
   p.k_rank_stride = k_rank_stride;
   p.v_rank_stride = v_rank_stride;
+  p.drop_rate = drop_rate;
+  p.drop_seed = drop_seed;
   {
     const int osz = dtype_size(out_dtype);
     p.out_vec_ok = (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (out_strides[0] * osz) % 16 == 0 &&
@@ -214,6 +217,18 @@ int wf_sparse_attention(const void* q, const void* k, const void* v, int32_t dty
                         const int64_t* out_strides, int32_t* status, void* stream) {
   return attention_impl(q, k, v, dtype, idx, B, H, Tq, Tk, D, K, q_strides, k_strides, v_strides, idx_strides,
                         scale, flags, out, out_dtype, out_strides, status, stream, 0, 1, 0, 0);
+}
+
+int wf_sparse_attention_dropout(const void* q, const void* k, const void* v, int32_t dtype, const int32_t* idx,
+                                int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t D, int32_t K,
+                                const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                                const int64_t* idx_strides, float scale, int32_t flags, float drop_rate,
+                                uint64_t drop_seed, void* out, int32_t out_dtype, const int64_t* out_strides,
+                                int32_t* status, void* stream) {
+  if (!(drop_rate >= 0.f && drop_rate < 1.f))
+    return fail(WF_ERR_INVALID_ARGUMENT, "drop_rate must be in [0, 1), got %g", (double)drop_rate);
+  return attention_impl(q, k, v, dtype, idx, B, H, Tq, Tk, D, K, q_strides, k_strides, v_strides, idx_strides,
+                        scale, flags, out, out_dtype, out_strides, status, stream, 0, 1, 0, 0, drop_rate, drop_seed);
 }
 
 int wf_sparse_attention_cyclic_kv(const void* q, const void* k, const void* v, int32_t dtype, const int32_t* idx,
@@ -460,7 +475,8 @@ int wf_sparse_attention_backward(const void* q, const void* k, const void* v, in
                                  int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t D, int32_t K,
                                  const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
                                  const int64_t* idx_strides, const void* dout, const int64_t* dout_strides, float scale,
-                                 int32_t flags, void* dq, void* dk, void* dv, int32_t grad_dtype,
+                                 int32_t flags, float drop_rate, uint64_t drop_seed, void* dq, void* dk, void* dv,
+                                 int32_t grad_dtype,
                                  const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
                                  void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
   int rc = check_attn(q, k, v, dtype, idx, B, H, Tq, Tk, D, K, q_strides, k_strides, v_strides, idx_strides, scale,
@@ -496,6 +512,10 @@ int wf_sparse_attention_backward(const void* q, const void* k, const void* v, in
   p.dq_vec_ok = vec_ok(dq, dq_strides);
   p.dk_vec_ok = vec_ok(dk, dk_strides);
   p.dv_vec_ok = vec_ok(dv, dv_strides);
+  if (!(drop_rate >= 0.f && drop_rate < 1.f))
+    return fail(WF_ERR_INVALID_ARGUMENT, "drop_rate must be in [0, 1), got %g", (double)drop_rate);
+  p.drop_rate = drop_rate;
+  p.drop_seed = drop_seed;
   p.status = status;
   rc = wf::launch_sparse_attention_backward(p, workspace, workspace_bytes, dtype, grad_dtype,
                                             static_cast<cudaStream_t>(stream));

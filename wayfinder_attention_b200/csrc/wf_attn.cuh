@@ -73,7 +73,7 @@ __device__ __forceinline__ int64_t kv_row_offset(const AttnParams& p, int j, int
 
 // CYC: keys live in rank-major gathered blocks (kv_world > 1); a separate
 // instantiation keeps the address arithmetic of the plain layout minimal.
-template <typename TI, typename TO, int D, int E, bool CYC>
+template <typename TI, typename TO, int D, int E, bool CYC, bool DROP>
 __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, int warps_per_block) {
   using V16 = Vec16<TI>;
   constexpr int VEC = V16::N;
@@ -193,6 +193,8 @@ __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, in
   float acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0.f;
+  const uint64_t drow = DROP ? (((uint64_t)b * p.H + (uint64_t)hc) * p.Tq + (uint64_t)t) * (uint64_t)K : 0;
+  const float inv_keep = DROP ? 1.0f / (1.0f - p.drop_rate) : 1.0f;
 #pragma unroll 1
   for (int k0 = 0; k0 < K; k0 += kU) {
     uint4 raw[kU][NV];
@@ -202,6 +204,7 @@ __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, in
       const bool in = k0 + u < K;
       const int j = in ? sI[k0 + u] : kMasked;
       pw[u] = in ? myP[k0 + u] : 0.f;
+      if (DROP && in) pw[u] *= dropout_scale(p.drop_seed, drow + (uint64_t)(k0 + u), p.drop_rate, inv_keep);
 #pragma unroll
       for (int v = 0; v < NV; ++v)
         raw[u][v] = (j >= 0 && hv) ? ldg16(vb + kv_row_offset<CYC>(p, j, p.vst, p.v_rank_stride) + v * L * VEC) : make_uint4(0, 0, 0, 0);
@@ -244,7 +247,9 @@ int launch_t(const AttnParams& p, cudaStream_t stream) {
   int wpb = (int)(kSmemBudget / per_warp);
   wpb = wpb < 1 ? 1 : (wpb > 8 ? 8 : wpb);
   const size_t smem = per_warp * wpb;
-  auto kern = p.kv_world > 1 ? sparse_attn_kernel<TI, TO, D, E, true> : sparse_attn_kernel<TI, TO, D, E, false>;
+  auto kern = p.kv_world > 1 ? sparse_attn_kernel<TI, TO, D, E, true, false>
+              : p.drop_rate > 0.f ? sparse_attn_kernel<TI, TO, D, E, false, true>
+                                  : sparse_attn_kernel<TI, TO, D, E, false, false>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;

@@ -178,10 +178,16 @@ __global__ void __launch_bounds__(256) attn_bwd_query_kernel(const AttnBwdParams
   __syncwarp();
   // 2. dp_k = <dO, v_k>
   gather_dot(vb, p.vst, gf, myD, false);
+  // With dropout the forward weighted v_k by p_k z_k, z_k = keep / (1 - rate): the
+  // gradient with respect to p_k is dp_k z_k, and dv uses p_k z_k.
+  const bool drop = p.drop_rate > 0.f;
+  const uint64_t drow = (((uint64_t)b * p.H + (uint64_t)hc) * p.Tq + (uint64_t)t) * (uint64_t)K;
+  const float inv_keep = drop ? 1.0f / (1.0f - p.drop_rate) : 1.0f;
   float dsum = 0.f;
   for (int s = sub; s < K; s += L) {
     const float pk = myP[s] * inv;
     myP[s] = pk;
+    if (drop) myD[s] *= dropout_scale(p.drop_seed, drow + (uint64_t)s, p.drop_rate, inv_keep);
     dsum = fmaf(pk, myD[s], dsum);
   }
 #pragma unroll
@@ -194,7 +200,7 @@ __global__ void __launch_bounds__(256) attn_bwd_query_kernel(const AttnBwdParams
     const float dsk = p.scale * pk * (myD[s] - dsum);
     myD[s] = dsk;
     if (hv) {
-      Pg[(int64_t)s * p.H + h] = pk;
+      Pg[(int64_t)s * p.H + h] = drop ? pk * dropout_scale(p.drop_seed, drow + (uint64_t)s, p.drop_rate, inv_keep) : pk;
       Dg[(int64_t)s * p.H + h] = dsk;
     }
   }

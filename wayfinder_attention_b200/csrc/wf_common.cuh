@@ -96,4 +96,21 @@ __device__ __forceinline__ unsigned lanemask_lt() {
   return m;
 }
 
+// Attention-probability dropout: uniform in [0, 1) for element `idx` of the
+// (B, H, Tq, K) probability tensor under `seed`, from the SplitMix64 output
+// function (Steele, Lea and Flood, "Fast splittable pseudorandom number
+// generators", OOPSLA 2014) applied to seed + (idx + 1) * golden-ratio increment;
+// 24 high bits.  Counter-based, so the backward recomputes the forward's mask.
+__host__ __device__ __forceinline__ float dropout_uniform(uint64_t seed, uint64_t idx) {
+  uint64_t z = seed + (idx + 1ull) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
+// Multiplier of a kept (1 / (1 - rate)) or dropped (0) probability.
+__device__ __forceinline__ float dropout_scale(uint64_t seed, uint64_t idx, float rate, float inv_keep) {
+  return dropout_uniform(seed, idx) >= rate ? inv_keep : 0.f;
+}
+
 }  // namespace wf

@@ -52,6 +52,10 @@ struct AttnParams {
   int kv_tile, kv_world;
   int64_t k_rank_stride, v_rank_stride;
   int32_t* status;       // nullable; bit 0 set on an out-of-range index
+  // Attention-probability dropout (training): rate in [0, 1), 0 = off.  Element
+  // (b, h, t, k) is kept when dropout_uniform(seed, ((b*H + h)*Tq + t)*K + k) >= rate.
+  float drop_rate;
+  uint64_t drop_seed;
 };
 
 // Returns a cudaError_t; a negative value means "unsupported configuration"
@@ -104,6 +108,8 @@ struct AttnBwdParams {
   float scale;
   int mask_negative;
   int dq_vec_ok, dk_vec_ok, dv_vec_ok;
+  float drop_rate;       // the forward's dropout (see AttnParams); 0 = off
+  uint64_t drop_seed;
   float* P;      // [B][Tq][K][H] softmax probabilities (workspace)
   float* DS;     // [B][Tq][K][H] scale * ds (workspace)
   int32_t* cnt;  // [B][Tk] per-key counts, then fill cursors (workspace)

@@ -66,6 +66,8 @@ def _launch_attention(
     out_dtype: torch.dtype | None,
     status: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
+    drop_rate: float = 0.0,
+    drop_seed: int = 0,
 ) -> torch.Tensor:
     dev = _lib.require_cuda(q, k, v, indices)
     lib = _lib.load_library()
@@ -84,20 +86,30 @@ def _launch_attention(
     q, k, v = _attn_operand(q), _attn_operand(k), _attn_operand(v)
     if status is not None and (status.dtype != torch.int32 or not status.is_cuda):
         raise ValueError("status must be an int32 CUDA tensor")
+    flags = _lib.WF_ATTN_MASK_NEGATIVE if mask_negative else 0
+    st = status.data_ptr() if status is not None else None
     with torch.cuda.device(dev):
-        rc = lib.wf_sparse_attention(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.dtype_code(q.dtype), indices.data_ptr(),
-            B, H, Tq, Tk, D, K,
-            _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(indices),
-            float(scale), _lib.WF_ATTN_MASK_NEGATIVE if mask_negative else 0,
-            out.data_ptr(), _lib.dtype_code(out.dtype), _lib.strides(out),
-            status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
-        )
+        if drop_rate > 0.0:
+            rc = lib.wf_sparse_attention_dropout(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.dtype_code(q.dtype), indices.data_ptr(),
+                B, H, Tq, Tk, D, K, _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(indices),
+                float(scale), flags, float(drop_rate), int(drop_seed), out.data_ptr(), _lib.dtype_code(out.dtype),
+                _lib.strides(out), st, _lib.stream_ptr(dev),
+            )
+        else:
+            rc = lib.wf_sparse_attention(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.dtype_code(q.dtype), indices.data_ptr(),
+                B, H, Tq, Tk, D, K,
+                _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(indices),
+                float(scale), flags, out.data_ptr(), _lib.dtype_code(out.dtype), _lib.strides(out),
+                st, _lib.stream_ptr(dev),
+            )
     _lib.check(rc)
     return out
 
 
-def _launch_attention_backward(q, k, v, indices, dout, scale, mask_negative, status=None):
+def _launch_attention_backward(q, k, v, indices, dout, scale, mask_negative, status=None, drop_rate=0.0,
+                               drop_seed=0):
     """(dq, dk, dv) of the sparse attention via ``wf_sparse_attention_backward``."""
     dev = _lib.require_cuda(q, k, v, indices, dout)
     lib = _lib.load_library()
@@ -116,7 +128,7 @@ def _launch_attention_backward(q, k, v, indices, dout, scale, mask_negative, sta
             q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.dtype_code(q.dtype), indices.data_ptr(),
             B, H, Tq, Tk, D, K, _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(indices),
             dout.data_ptr(), _lib.strides(dout), float(scale), _lib.WF_ATTN_MASK_NEGATIVE if mask_negative else 0,
-            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _lib.dtype_code(q.dtype), _lib.strides(dq),
+            float(drop_rate), int(drop_seed), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _lib.dtype_code(q.dtype), _lib.strides(dq),
             _lib.strides(dk), _lib.strides(dv), ws.data_ptr(), ws.numel(),
             status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
         )
@@ -128,18 +140,21 @@ class _SparseMeatFunction(torch.autograd.Function):
     """Sparse attention with a backward (``wf_sparse_attention_backward``); indices get no gradient."""
 
     @staticmethod
-    def forward(ctx, q, k, v, indices, scale, mask_negative, out_dtype):
-        out = _launch_attention(q, k, v, indices, scale, mask_negative=mask_negative, out_dtype=out_dtype)
+    def forward(ctx, q, k, v, indices, scale, mask_negative, out_dtype, drop_rate, drop_seed):
+        out = _launch_attention(q, k, v, indices, scale, mask_negative=mask_negative, out_dtype=out_dtype,
+                                drop_rate=drop_rate, drop_seed=drop_seed)
         ctx.save_for_backward(q, k, v, indices)
         ctx.scale = scale
         ctx.mask_negative = mask_negative
+        ctx.drop = (drop_rate, drop_seed)
         return out
 
     @staticmethod
     def backward(ctx, dout):
         q, k, v, indices = ctx.saved_tensors
-        dq, dk, dv = _launch_attention_backward(q, k, v, indices, dout, ctx.scale, ctx.mask_negative)
-        return dq, dk, dv, None, None, None, None
+        dq, dk, dv = _launch_attention_backward(q, k, v, indices, dout, ctx.scale, ctx.mask_negative,
+                                                drop_rate=ctx.drop[0], drop_seed=ctx.drop[1])
+        return dq, dk, dv, None, None, None, None, None, None
 
 
 def sparse_meat_attention(
@@ -154,6 +169,8 @@ def sparse_meat_attention(
     out_dtype: torch.dtype | None = None,
     mask_negative: bool = False,
     status: torch.Tensor | None = None,
+    dropout_p: float = 0.0,
+    dropout_seed: int | None = None,
 ) -> torch.Tensor:
     """Multi-head sparse attention on pre-selected indices shared across heads.
 
@@ -163,7 +180,9 @@ def sparse_meat_attention(
     indexing unless ``mask_negative`` is set, in which case they are excluded
     from the softmax.  Differentiable in q, k and v when autograd records (the
     reference's gather path is too, ``fused_sparse.py:64-94``); the indices carry
-    no gradient.
+    no gradient.  ``dropout_p`` > 0 drops attention probabilities like the reference's
+    training path (``models/attention.py:50-54``); the mask comes from ``dropout_seed``
+    (drawn from torch's generator when None) and is recomputed by the backward.
     """
     del method, config
     _check_meat_shapes(q, k, v)
@@ -171,13 +190,18 @@ def sparse_meat_attention(
         q, k, v = q.float(), k.float(), v.float()
     if indices.dtype != torch.int32:
         indices = indices.to(torch.int32)
+    if not 0.0 <= dropout_p < 1.0:
+        raise ValueError(f"dropout_p must be in [0, 1), got {dropout_p}")
+    seed = 0
+    if dropout_p > 0.0:
+        seed = int(dropout_seed) if dropout_seed is not None else int(torch.randint(0, 2 ** 62, (1,)).item())
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
         if status is not None:
             raise ValueError("status is not supported on the differentiable path")
-        return _SparseMeatFunction.apply(q, k, v, indices, scale, mask_negative, out_dtype)
+        return _SparseMeatFunction.apply(q, k, v, indices, scale, mask_negative, out_dtype, float(dropout_p), seed)
     with torch.no_grad():
         return _launch_attention(q, k, v, indices, scale, mask_negative=mask_negative, out_dtype=out_dtype,
-                                 status=status)
+                                 status=status, drop_rate=float(dropout_p), drop_seed=seed)
 
 
 def sparse_meat_attention_reference(q, k, v, indices, scale):
