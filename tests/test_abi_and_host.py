@@ -181,7 +181,9 @@ def test_workspace_query():
     lib = _lib.load_library()
     assert lib.wf_causal_topk_workspace_bytes(1, 16384, 16384, 32, 128, _lib.WF_DTYPE_BF16) == 16384 * (4 * 256 * 8 + 16)
     assert lib.wf_causal_topk_workspace_bytes(2, 100, 100, 32, 64, _lib.WF_DTYPE_F16) == 200 * (4 * 256 * 8 + 16)
-    assert lib.wf_causal_topk_workspace_bytes(1, 2048, 2048, 32, 128, _lib.WF_DTYPE_F32) == 0  # CUDA-core path
+    # fp32 addresses: the lists plus bf16 copies of the query and key addresses
+    assert lib.wf_causal_topk_workspace_bytes(1, 2048, 2048, 32, 128, _lib.WF_DTYPE_F32) == (
+        2048 * (4 * 256 * 8 + 16) + (2048 + 2048) * 32 * 2 + 256)
     # K <= 256 on tensor cores: lists of 384 slots above K = 128
     assert lib.wf_causal_topk_workspace_bytes(1, 2048, 2048, 32, 256, _lib.WF_DTYPE_BF16) == 2048 * (4 * 384 * 8 + 16)
     # large batches run in slices of 65536 // T batch elements that reuse one workspace

@@ -352,6 +352,9 @@ def test_decoder_prefill_smoke(cuda_device):
         (64, 200, 2500, 1, torch.float16, False),
         (32, 256, 300, 1, torch.bfloat16, False),   # short rows: K_eff = 256 with pads
         (32, 128, 8192, 10, torch.bfloat16, True),  # 8 + 2 batch elements: two workspace slices
+        (32, 128, 2048, 1, torch.float32, False),   # cfg1: fp32 addresses via bf16 copies + fp32 rescoring
+        (16, 64, 3000, 2, torch.float32, True),
+        (64, 256, 1500, 1, torch.float32, False),
     ],
 )
 def test_tensor_core_topk_equals_cuda_core(R, K, T, B, dtype, clustered, cuda_device, monkeypatch):

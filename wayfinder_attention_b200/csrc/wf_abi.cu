@@ -138,10 +138,10 @@ int wf_max_top_k(void) { return wf::topk_max_k(); }
 size_t wf_causal_topk_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, int32_t R, int32_t top_k, int32_t dtype) {
   if (B <= 0 || Tq <= 0 || Tk <= 0 || top_k <= 0) return 0;
   const int64_t k_eff = top_k < Tk ? top_k : Tk;
-  if (dtype != WF_DTYPE_BF16 && dtype != WF_DTYPE_F16) return 0;
+  if (!valid_dtype(dtype)) return 0;
   if (R != 16 && R != 32 && R != 64) return 0;
   if (Tk > 65536) return 0;
-  return wf::topk_tc_workspace_bytes(B, Tq, (int)k_eff);
+  return wf::topk_tc_workspace_bytes(B, Tq, Tk, R, (int)k_eff, dtype);
 }
 
 int wf_causal_topk(const void* q_addr, const void* k_addr, int32_t dtype, int64_t B, int64_t Tq,

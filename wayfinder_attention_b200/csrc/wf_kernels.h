@@ -73,7 +73,7 @@ size_t noalloc_scratch_capacity();
 int noalloc_scratch(void** out);
 
 // Workspace bytes the tensor-core path needs for B*Tq query rows (0 if K > 128).
-size_t topk_tc_workspace_bytes(int64_t B, int64_t Tq, int K);
+size_t topk_tc_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, int R, int K, int dtype);
 
 // Shared-memory bytes the top-K kernel needs for (R, K); 0 if unsupported.
 size_t topk_smem_bytes(int R, int K);

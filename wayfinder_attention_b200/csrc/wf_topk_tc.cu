@@ -99,6 +99,10 @@ struct TcParams {
   uint64_t* ws;      // [B*Tq][kLists][KW] candidate composites (key << 32 | ~index)
   int32_t* ws_cnt;   // [B*Tq][kLists] candidate counts
   const int32_t* lim;  // optional [B][Tq] per-row key limits (see TopkParams)
+  // fp32 addresses: the MMAs read bf16 copies; admitted keys are rescored from these
+  const float* qf;
+  const float* kf;
+  int64_t fqsb, fqst, fksb, fkst;
 };
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -164,7 +168,29 @@ __device__ __forceinline__ float dot_swizzled(const unsigned char* qtile, int qr
   return acc;
 }
 
-template <typename TI, int R, int KW>
+// Exact fp32 score from the original fp32 rows (sequential FMA over d, as the
+// CUDA-core kernel and dot_swizzled compute it).
+template <int R>
+__device__ __forceinline__ float dot_f32_rows(const float* qrow, const float* krow) {
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < R / 4; ++c) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(qrow) + c);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(krow) + c);
+    acc = fmaf(a.x, b.x, acc);
+    acc = fmaf(a.y, b.y, acc);
+    acc = fmaf(a.z, b.z, acc);
+    acc = fmaf(a.w, b.w, acc);
+  }
+  return acc;
+}
+
+// F32: fp32 addresses.  The tensor cores score bf16 copies (TI = bf16); every
+// product is then off by at most 2^-8 |q_d k_d| (two bf16 roundings), so the
+// admission margin widens to 2^-6 sum|q| max|k| (twice the worst-case score error,
+// with slack for max|k| being taken from the rounded keys), and admitted keys are
+// rescored from the fp32 rows: the result is exact with respect to fp32 scores.
+template <typename TI, int R, int KW, bool F32>
 __global__ void __launch_bounds__(kThreads, 1)
     causal_topk_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                           const TcParams p) {
@@ -313,13 +339,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int pair_bar = 1 + qd;   // named barrier of the two warps of this quadrant
     float qabs = 0.f;
     if (row_ok) {
-      const TI* qrow = reinterpret_cast<const TI*>(p.q) + (int64_t)b * p.qsb + (int64_t)(l0 + r) * p.qst;
+      if constexpr (F32) {
+        const float* qrow = p.qf + (int64_t)b * p.fqsb + (int64_t)(l0 + r) * p.fqst;
 #pragma unroll
-      for (int c = 0; c < R / 8; ++c) {
-        float f[8];
-        Vec16<TI>::unpack(ldg16(qrow + c * 8), f);
+        for (int c = 0; c < R; ++c) qabs += fabsf(qrow[c]);
+      } else {
+        const TI* qrow = reinterpret_cast<const TI*>(p.q) + (int64_t)b * p.qsb + (int64_t)(l0 + r) * p.qst;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) qabs += fabsf(f[e]);
+        for (int c = 0; c < R / 8; ++c) {
+          float f[8];
+          Vec16<TI>::unpack(ldg16(qrow + c * 8), f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) qabs += fabsf(f[e]);
+        }
       }
     }
     {
@@ -480,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_arrive_peer(map_peer(kbar, peer));
     if (!warp_wait_cluster(kbar, 0)) { ok = false; why |= 1024; }
     const float kpair = fmaxf(__uint_as_float(*kmax_own_s), __uint_as_float(*kmax_in_s));
-    const float eps = kEpsScale * qabs * kpair;
+    const float eps = (F32 ? 1.0f / 64.0f : kEpsScale) * qabs * kpair;
     float lim = theta > -INFINITY ? theta - eps : -INFINITY;
 
     PROF_T(tbe);
@@ -499,7 +531,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int e = lane; e < qsize; e += 32) {
         const uint32_t ent = queue[e];
         const int lr = ent & 31, jj = (ent >> 5) & 127, dest = (int)(ent >> 12);
-        const float ex = dot_swizzled<TI, ROWB>(qs, 32 * qd + lr, stage, jj);
+        float ex;
+        if constexpr (F32)
+          ex = dot_f32_rows<R>(p.qf + (int64_t)b * p.fqsb + (int64_t)(l0 + 32 * qd + lr) * p.fqst,
+                               p.kf + (int64_t)b * p.fksb + (int64_t)(c * kN + jj) * p.fkst);
+        else
+          ex = dot_swizzled<TI, ROWB>(qs, 32 * qd + lr, stage, jj);
         p.ws[(((row0 + lr) * 2 + rank) * 2 + hf) * KW + dest] =
             ((uint64_t)ordered_key(ex) << 32) | (uint32_t)(~(uint32_t)(c * kN + jj));
       }
@@ -801,11 +838,27 @@ int64_t batch_per_pass(int64_t B, int64_t Tq) {
 
 size_t ws_bytes_per_row(int K) { return (size_t)kLists * list_capacity(K) * sizeof(uint64_t) + kLists * sizeof(int32_t); }
 
-template <typename TI, int R, int KW, int SE>
+// bf16 copies of fp32 address rows (F32 path): dst[b][t][r] contiguous.
+__global__ void shadow_bf16_kernel(const float* src, int64_t sb, int64_t st, int nb, int T, int R,
+                                   __nv_bfloat16* dst) {
+  const int64_t n = (int64_t)nb * T * R;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(e % R);
+    const int64_t bt = e / R;
+    const int t = (int)(bt % T), b = (int)(bt / T);
+    dst[e] = __float2bfloat16_rn(src[(int64_t)b * sb + (int64_t)t * st + r]);
+  }
+}
+
+size_t shadow_bytes_pass(int64_t bpp, int64_t Tq, int64_t Tk, int R) {
+  return (size_t)bpp * (Tq + Tk) * R * 2 + 256;
+}
+
+template <typename TI, int R, int KW, int SE, bool F32>
 int launch_t(const TopkParams& p, cudaStream_t stream) {
   using L = Layout<R, KW>;
   if (L::smem > kMaxSmem) return -1;
-  auto kern = causal_topk_tc_kernel<TI, R, KW>;
+  auto kern = causal_topk_tc_kernel<TI, R, KW, F32>;
   static bool configured[kMaxDevices] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -818,23 +871,42 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
   const bool bf16 = !std::is_same<TI, __half>::value;
   const int64_t bpp = batch_per_pass(p.B, p.Tq);
   const size_t rows_pass = (size_t)bpp * p.Tq;
-  const size_t need = rows_pass * ws_bytes_per_row(p.K);
+  const size_t lists = rows_pass * ws_bytes_per_row(p.K);
+  const size_t need = lists + (F32 ? shadow_bytes_pass(bpp, p.Tq, p.Tk, R) : 0);
   if (!p.ws || p.ws_bytes < need || reinterpret_cast<uintptr_t>(p.ws) % 16) return -3;
   uint64_t* ws = reinterpret_cast<uint64_t*>(p.ws);
   int32_t* ws_cnt = reinterpret_cast<int32_t*>(ws + rows_pass * kLists * KW);
-  const size_t esz = 2;
+  __nv_bfloat16* shq = reinterpret_cast<__nv_bfloat16*>(
+      (reinterpret_cast<uintptr_t>(static_cast<char*>(p.ws) + lists) + 255) & ~uintptr_t(255));
+  __nv_bfloat16* shk = shq + (size_t)bpp * p.Tq * R;
+  const size_t esz = F32 ? 4 : 2;
   // Batch slices run one after the other on the stream and reuse the workspace.
   for (int64_t b0 = 0; b0 < p.B; b0 += bpp) {
     const int nb = (int)(p.B - b0 < bpp ? p.B - b0 : bpp);
     const void* q = static_cast<const char*>(p.q) + (size_t)(b0 * p.qsb) * esz;
     const void* k = static_cast<const char*>(p.k) + (size_t)(b0 * p.ksb) * esz;
     CUtensorMap qmap, kmap;
-    if (!make_map(&qmap, q, bf16, R, p.Tq, nb, p.qst, p.qsb, kM)) return -1;
-    if (!make_map(&kmap, k, bf16, R, p.Tk, nb, p.kst, p.ksb, kN)) return -1;
     TcParams t{};
-    t.q = q;
-    t.qsb = p.qsb;
-    t.qst = p.qst;
+    if constexpr (F32) {
+      const unsigned gq = (unsigned)(((int64_t)nb * p.Tq * R + 255) / 256 < 148 * 8 ? ((int64_t)nb * p.Tq * R + 255) / 256 : 148 * 8);
+      const unsigned gk = (unsigned)(((int64_t)nb * p.Tk * R + 255) / 256 < 148 * 8 ? ((int64_t)nb * p.Tk * R + 255) / 256 : 148 * 8);
+      shadow_bf16_kernel<<<gq, 256, 0, stream>>>(static_cast<const float*>(q), p.qsb, p.qst, nb, p.Tq, R, shq);
+      shadow_bf16_kernel<<<gk, 256, 0, stream>>>(static_cast<const float*>(k), p.ksb, p.kst, nb, p.Tk, R, shk);
+      if (!make_map(&qmap, shq, true, R, p.Tq, nb, R, (int64_t)p.Tq * R, kM)) return -1;
+      if (!make_map(&kmap, shk, true, R, p.Tk, nb, R, (int64_t)p.Tk * R, kN)) return -1;
+      t.qf = static_cast<const float*>(q);
+      t.kf = static_cast<const float*>(k);
+      t.fqsb = p.qsb; t.fqst = p.qst; t.fksb = p.ksb; t.fkst = p.kst;
+      t.q = shq;
+      t.qsb = (int64_t)p.Tq * R;
+      t.qst = R;
+    } else {
+      if (!make_map(&qmap, q, bf16, R, p.Tq, nb, p.qst, p.qsb, kM)) return -1;
+      if (!make_map(&kmap, k, bf16, R, p.Tk, nb, p.kst, p.ksb, kN)) return -1;
+      t.q = q;
+      t.qsb = p.qsb;
+      t.qst = p.qst;
+    }
     t.B = nb; t.Tq = p.Tq; t.Tk = p.Tk; t.K = p.K;
     t.pad_mode = p.pad_mode;
     t.rt = p.rt; t.rs = p.rs; t.r0 = p.r0;
@@ -874,21 +946,21 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
   return 0;
 }
 
-template <typename TI, int R>
+template <typename TI, int R, bool F32>
 int launch_r(const TopkParams& p, cudaStream_t s) {
-  if (p.K <= 32) return launch_t<TI, R, 256, 1>(p, s);
-  if (p.K <= 64) return launch_t<TI, R, 256, 2>(p, s);
-  if (p.K <= 128) return launch_t<TI, R, 256, 4>(p, s);
-  if (p.K <= 256) return launch_t<TI, R, 384, 8>(p, s);
+  if (p.K <= 32) return launch_t<TI, R, 256, 1, F32>(p, s);
+  if (p.K <= 64) return launch_t<TI, R, 256, 2, F32>(p, s);
+  if (p.K <= 128) return launch_t<TI, R, 256, 4, F32>(p, s);
+  if (p.K <= 256) return launch_t<TI, R, 384, 8, F32>(p, s);
   return -1;
 }
 
-template <typename TI>
+template <typename TI, bool F32>
 int launch_ti(const TopkParams& p, cudaStream_t s) {
   switch (p.R) {
-    case 16: return launch_r<TI, 16>(p, s);
-    case 32: return launch_r<TI, 32>(p, s);
-    case 64: return launch_r<TI, 64>(p, s);
+    case 16: return launch_r<TI, 16, F32>(p, s);
+    case 32: return launch_r<TI, 32, F32>(p, s);
+    case 64: return launch_r<TI, 64, F32>(p, s);
     default: return -1;
   }
 }
@@ -896,27 +968,31 @@ int launch_ti(const TopkParams& p, cudaStream_t s) {
 }  // namespace
 
 bool topk_tc_supported(const TopkParams& p, int dtype) {
-  if (dtype != kBF16 && dtype != kF16) return false;
+  if (dtype != kBF16 && dtype != kF16 && dtype != kF32) return false;
   if (p.R != 16 && p.R != 32 && p.R != 64) return false;
   if (p.K > 256 || p.Tk > 65536 || p.B > 65535) return false;
   const size_t sm = tc_smem(p.R, p.K);
   if (sm == 0 || sm > kMaxSmem) return false;
   if (p.qsr != 1 || p.ksr != 1) return false;
   if ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.k)) % 16) return false;
-  if ((p.qst * 2) % 16 || (p.kst * 2) % 16 || (p.qsb * 2) % 16 || (p.ksb * 2) % 16) return false;
+  const int esz = dtype == kF32 ? 4 : 2;  // fp32: rows read as float4 for the rescoring
+  if ((p.qst * esz) % 16 || (p.kst * esz) % 16 || (p.qsb * esz) % 16 || (p.ksb * esz) % 16) return false;
   const bool identity = p.rs == 1 && p.r0 == 0;
   if (!identity && p.rt % kM) return false;
   return encode_fn() != nullptr;
 }
 
-size_t topk_tc_workspace_bytes(int64_t B, int64_t Tq, int K) {
+size_t topk_tc_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, int R, int K, int dtype) {
   if (K > 256 || B <= 0 || Tq <= 0) return 0;
-  return (size_t)batch_per_pass(B, Tq) * Tq * ws_bytes_per_row(K);
+  const int64_t bpp = batch_per_pass(B, Tq);
+  const size_t lists = (size_t)bpp * Tq * ws_bytes_per_row(K);
+  return dtype == kF32 ? lists + shadow_bytes_pass(bpp, Tq, Tk, R) : lists;
 }
 
 int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream) {
-  if (dtype == kBF16) return launch_ti<__nv_bfloat16>(p, stream);
-  if (dtype == kF16) return launch_ti<__half>(p, stream);
+  if (dtype == kBF16) return launch_ti<__nv_bfloat16, false>(p, stream);
+  if (dtype == kF16) return launch_ti<__half, false>(p, stream);
+  if (dtype == kF32) return launch_ti<__nv_bfloat16, true>(p, stream);
   return -1;
 }
 
