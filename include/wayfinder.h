@@ -173,6 +173,24 @@ WF_API int wf_sparse_attention_dropout(const void* q, const void* k, const void*
                                        int32_t out_dtype, const int64_t* out_strides, int32_t* status, void* stream);
 
 /*
+ * wf_sparse_attention_cyclic_kv with the gathered K/V stored chunk by chunk, so a
+ * rank can attend with the chunks that have already arrived (no counterpart in the
+ * reference).  Each rank's local rows are split into chunks of kv_chunk_rows (a
+ * multiple of kv_row_tile dividing Tk / kv_world); block (chunk c, rank r) holds
+ * local rows [c * kv_chunk_rows, (c + 1) * kv_chunk_rows) of rank r and starts
+ * (c * kv_world + r) * k_block_stride (v_block_stride) elements after k (v), whose
+ * strides describe one block as (B, H, kv_chunk_rows, D).  At most 64 blocks.
+ */
+WF_API int wf_sparse_attention_cyclic_kv_chunked(const void* q, const void* k, const void* v, int32_t dtype,
+                                                 const int32_t* idx, int64_t B, int64_t H, int64_t Tq, int64_t Tk,
+                                                 int32_t D, int32_t K, const int64_t* q_strides,
+                                                 const int64_t* k_strides, const int64_t* v_strides,
+                                                 const int64_t* idx_strides, float scale, int32_t flags, void* out,
+                                                 int32_t out_dtype, const int64_t* out_strides, int32_t kv_row_tile,
+                                                 int32_t kv_world, int32_t kv_chunk_rows, int64_t k_block_stride,
+                                                 int64_t v_block_stride, int32_t* status, void* stream);
+
+/*
  * Retrieval + attention in one call.  Replaces fused_sparse_attention()
  * (routing_attention/kernels/fused_sparse.py:327-356): wf_causal_topk into idx_out,
  * then wf_sparse_attention over it (masking pads when pad_mode == WF_PAD_MASKED).

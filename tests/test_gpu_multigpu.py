@@ -30,7 +30,7 @@ SCRIPT = textwrap.dedent(
     qkv = [torch.randn(B, T, H, D, generator=g, device=dev).bfloat16() for _ in range(3)]
     full_out, full_idx = fused_sparse_attention(qa, ka, *(t.transpose(1, 2) for t in qkv), K, D ** -0.5)
     rows = torch.from_numpy(local_rows(T, world, rank, tile)).to(dev)
-    op = SequenceShardedAttention(K, D ** -0.5, tile=tile)
+    op = SequenceShardedAttention(K, D ** -0.5, tile=tile, chunks=8)  # 8 K/V chunks of 256 local rows
     out, idx = op(qa[:, rows].contiguous(), ka[:, rows].contiguous(),
                   *(t[:, rows].contiguous().transpose(1, 2) for t in qkv))
     ok = torch.equal(idx, full_idx[:, rows]) and torch.equal(out, full_out[:, :, rows])

@@ -47,6 +47,7 @@ EXPORTED_SYMBOLS = (
     "wf_causal_topk_key_mask",
     "wf_causal_topk_key_mask_workspace_bytes",
     "wf_sparse_attention_dropout",
+    "wf_sparse_attention_cyclic_kv_chunked",
 )
 
 _DTYPE_CODES = {
@@ -88,6 +89,11 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.wf_sparse_attention_cyclic_kv.argtypes = [
         _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i32, _i32,
         _i64p, _i64p, _i64p, _i64p, _f32, _i32, _vp, _i32, _i64p, _i32, _i32, _i64, _i64, _vp, _vp,
+    ]
+    lib.wf_sparse_attention_cyclic_kv_chunked.restype = ctypes.c_int
+    lib.wf_sparse_attention_cyclic_kv_chunked.argtypes = [
+        _vp, _vp, _vp, _i32, _vp, _i64, _i64, _i64, _i64, _i32, _i32,
+        _i64p, _i64p, _i64p, _i64p, _f32, _i32, _vp, _i32, _i64p, _i32, _i32, _i32, _i64, _i64, _vp, _vp,
     ]
     lib.wf_fused_sparse_attention.restype = ctypes.c_int
     lib.wf_fused_sparse_attention.argtypes = [

@@ -177,7 +177,7 @@ int attention_impl(const void* q, const void* k, const void* v, int32_t dtype, c
                    const int64_t* k_strides, const int64_t* v_strides, const int64_t* idx_strides, float scale,
                    int32_t flags, void* out, int32_t out_dtype, const int64_t* out_strides, int32_t* status,
                    void* stream, int32_t kv_tile, int32_t kv_world, int64_t k_rank_stride, int64_t v_rank_stride,
-                   float drop_rate = 0.f, uint64_t drop_seed = 0) {
+                   float drop_rate = 0.f, uint64_t drop_seed = 0, int32_t kv_chunk_rows = 0) {
   int rc = check_attn(q, k, v, dtype, idx, B, H, Tq, Tk, D, K, q_strides, k_strides, v_strides, idx_strides,
                       scale, flags, out, out_dtype, out_strides);
   if (rc) return rc;
@@ -199,6 +199,7 @@ int attention_impl(const void* q, const void* k, const void* v, int32_t dtype, c
   p.v_rank_stride = v_rank_stride;
   p.drop_rate = drop_rate;
   p.drop_seed = drop_seed;
+  p.kv_chunk_rows = kv_chunk_rows;
   {
     const int osz = dtype_size(out_dtype);
     p.out_vec_ok = (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (out_strides[0] * osz) % 16 == 0 &&
@@ -250,6 +251,34 @@ int wf_sparse_attention_cyclic_kv(const void* q, const void* k, const void* v, i
   return attention_impl(q, k, v, dtype, idx, B, H, Tq, Tk, D, K, q_strides, k_strides, v_strides, idx_strides,
                         scale, flags, out, out_dtype, out_strides, status, stream, kv_row_tile, kv_world,
                         k_rank_stride, v_rank_stride);
+}
+
+int wf_sparse_attention_cyclic_kv_chunked(const void* q, const void* k, const void* v, int32_t dtype,
+                                          const int32_t* idx, int64_t B, int64_t H, int64_t Tq, int64_t Tk, int32_t D,
+                                          int32_t K, const int64_t* q_strides, const int64_t* k_strides,
+                                          const int64_t* v_strides, const int64_t* idx_strides, float scale,
+                                          int32_t flags, void* out, int32_t out_dtype, const int64_t* out_strides,
+                                          int32_t kv_row_tile, int32_t kv_world, int32_t kv_chunk_rows,
+                                          int64_t k_block_stride, int64_t v_block_stride, int32_t* status,
+                                          void* stream) {
+  if (kv_world < 1 || kv_row_tile < 1 || kv_chunk_rows < 1)
+    return fail(WF_ERR_INVALID_ARGUMENT, "kv_world, kv_row_tile and kv_chunk_rows must be >= 1");
+  if (Tk >= (int64_t(1) << 25)) return fail(WF_ERR_UNSUPPORTED, "Tk=%lld too large for the gathered key layout", (long long)Tk);
+  if (Tk % ((int64_t)kv_row_tile * kv_world))
+    return fail(WF_ERR_INVALID_ARGUMENT, "Tk=%lld is not a whole number of %d-row blocks on %d ranks", (long long)Tk,
+                kv_row_tile, kv_world);
+  const int64_t local = Tk / kv_world;
+  if (kv_chunk_rows % kv_row_tile || local % kv_chunk_rows)
+    return fail(WF_ERR_INVALID_ARGUMENT, "kv_chunk_rows=%d must be a multiple of kv_row_tile and divide the %lld local rows",
+                kv_chunk_rows, (long long)local);
+  if ((local / kv_chunk_rows) * kv_world > 64)
+    return fail(WF_ERR_UNSUPPORTED, "at most 64 (chunk, rank) blocks");
+  const int esz = dtype_size(dtype);
+  if ((k_block_stride * esz) % 16 || (v_block_stride * esz) % 16)
+    return fail(WF_ERR_UNSUPPORTED, "block strides must be multiples of 16 bytes");
+  return attention_impl(q, k, v, dtype, idx, B, H, Tq, Tk, D, K, q_strides, k_strides, v_strides, idx_strides,
+                        scale, flags, out, out_dtype, out_strides, status, stream, kv_row_tile, kv_world,
+                        k_block_stride, v_block_stride, 0.f, 0, kv_chunk_rows);
 }
 
 int wf_fused_sparse_attention(const void* q_addr, const void* k_addr, int32_t addr_dtype, int32_t R,

@@ -118,7 +118,14 @@ __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, in
       // rank-major gathered keys: rank r's rows follow each other, r < kv_world <= 64,
       // stored as r * 2^25 + local row (Tk < 2^25 is checked by the caller)
       const int blk = j / p.kv_tile;
-      j = ((blk % p.kv_world) << 25) | ((blk / p.kv_world) * p.kv_tile + j % p.kv_tile);
+      int blk_id = blk % p.kv_world;
+      int lr = (blk / p.kv_world) * p.kv_tile + j % p.kv_tile;
+      if (p.kv_chunk_rows > 0) {  // chunk-major: block (chunk, rank)
+        const int c = lr / p.kv_chunk_rows;
+        lr -= c * p.kv_chunk_rows;
+        blk_id += c * p.kv_world;
+      }
+      j = (blk_id << 25) | lr;
     }
     sI[s] = j;
   }

@@ -51,6 +51,10 @@ struct AttnParams {
   // (j / kv_tile / kv_world) * kv_tile + j % kv_tile.  kv_world = 1: identity.
   int kv_tile, kv_world;
   int64_t k_rank_stride, v_rank_stride;
+  // > 0: the gathered rows arrive in chunks of kv_chunk_rows local rows, stored
+  // chunk-major: local row lr of rank r is row lr % kv_chunk_rows of block
+  // (lr / kv_chunk_rows) * kv_world + r, blocks k/v_rank_stride apart.
+  int kv_chunk_rows;
   int32_t* status;       // nullable; bit 0 set on an out-of-range index
   // Attention-probability dropout (training): rate in [0, 1), 0 = off.  Element
   // (b, h, t, k) is kept when dropout_uniform(seed, ((b*H + h)*Tq + t)*K + k) >= rate.

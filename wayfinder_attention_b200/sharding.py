@@ -104,26 +104,41 @@ class SequenceShardedAttention:
     Rank r holds the query rows ``local_rows(T, W, r, tile)`` of the addresses and of
     q/k/v (in the module's (B, T, H, D) memory layout).  Every rank needs all key
     addresses and every K/V row up to its last query, so ``forward``:
-      1. all-gathers the key addresses (B*T*d_A elements, small) and starts the
-         K/V all-gather on a side stream;
+      1. all-gathers the key addresses (B*T*d_A elements, small) and, on a side
+         stream, the K/V rows in ``chunks`` chunks of local rows;
       2. runs the causal top-K of its own rows against all keys (row map of
          ``wf_causal_topk``) while K/V are in flight;
-      3. waits for K/V and runs the sparse attention of its rows.
-    The K/V all-gathers land rank-major and the attention kernel translates key
-    positions to (rank, local row) itself, so no reordering copy of K/V is made.
-    The only collectives are these all-gathers; nothing crosses ranks afterwards.
+      3. runs the attention of its rows chunk by chunk as the K/V chunks land: the
+         indices are causal, so local rows in chunk c read keys from chunks <= c of
+         every rank.  Chunk 0 goes last because the reference pads of rows t < K-1
+         (all in chunk 0 of rank 0, tile >= K) point at later keys.
+    The K/V all-gathers land chunk-major and the attention kernel maps key positions
+    to (chunk, rank, row) itself (``wf_sparse_attention_cyclic_kv_chunked``), so no
+    reordering copy of K/V is made.  The only collectives are these all-gathers.
     """
 
-    def __init__(self, top_k: int, scale: float, tile: int = 256, group=None, pad_mode: str = "reference"):
+    def __init__(self, top_k: int, scale: float, tile: int = 256, group=None, pad_mode: str = "reference",
+                 chunks: int | None = None):
         self.top_k = top_k
         self.scale = scale
         self.tile = tile
         self.group = group
         self.pad_mode = pad_mode
+        self.chunks = chunks
         # persistent per-shape gather buffers and side stream: a forward allocates nothing large
         self._kg = None
         self._vg = None
         self._side = None
+
+    def _n_chunks(self, Tl: int, world: int) -> int:
+        # Default: one chunk on 2 ranks, where retrieval already hides the gather
+        # (cfg4: 9.38 ms unchunked, 9.55 ms in 8 chunks), 8 chunks from 4 ranks up,
+        # where each rank receives (W-1)/W of K/V while its retrieval shrinks as 1/W.
+        want = self.chunks if self.chunks is not None else (1 if world <= 2 else 8)
+        c = max(1, min(want, 64 // world, Tl // self.tile))
+        while c > 1 and Tl % (c * self.tile):
+            c -= 1
+        return c
 
     def forward(self, q_addr_l: torch.Tensor, k_addr_l: torch.Tensor, q_l: torch.Tensor, k_l: torch.Tensor,
                 v_l: torch.Tensor, out_dtype: torch.dtype | None = None) -> tuple[torch.Tensor, torch.Tensor]:
@@ -136,33 +151,51 @@ class SequenceShardedAttention:
         rank = dist.get_rank(self.group)
         B, H, Tl, D = q_l.shape
         T = world * Tl
+        if self.top_k > self.tile:
+            raise ValueError(f"top_k={self.top_k} must not exceed the row tile {self.tile}")
+        C = self._n_chunks(Tl, world)
+        Tc = Tl // C
         main = torch.cuda.current_stream(q_l.device)
         if self._side is None or self._side.device != q_l.device:
             self._side = torch.cuda.Stream(device=q_l.device)
         side = self._side
+        shape = (C, world, B, Tc, H, D)
+        kt, vt = k_l.transpose(1, 2), v_l.transpose(1, 2)  # (B, Tl, H, D)
+        if self._kg is None or tuple(self._kg.shape) != shape or self._kg.dtype != k_l.dtype or self._kg.device != k_l.device:
+            self._kg = torch.empty(shape, dtype=k_l.dtype, device=k_l.device)
+            self._vg = torch.empty(shape, dtype=v_l.dtype, device=v_l.device)
+        k_g, v_g = self._kg, self._vg
         side.wait_stream(main)  # the previous call's attention has finished with the buffers
+        landed = []
         with torch.cuda.stream(side):
-            # rank-major (world, B, Tl, H, D): the attention kernel addresses it directly
-            self._kg = k_g = _all_gather_rows(k_l.transpose(1, 2), world, self.group, self._kg)
-            self._vg = v_g = _all_gather_rows(v_l.transpose(1, 2), world, self.group, self._vg)
+            for c in range(C):
+                rows = slice(c * Tc, (c + 1) * Tc)
+                _all_gather_rows(kt[:, rows], world, self.group, k_g[c])
+                _all_gather_rows(vt[:, rows], world, self.group, v_g[c])
+                ev = torch.cuda.Event()
+                ev.record(side)
+                landed.append(ev)
         k_addr = gather_sequence(k_addr_l, self.tile, self.group)  # small: reordered to global order
         idx = sharded_causal_topk(q_addr_l, k_addr, self.top_k, world, rank, self.tile, self.pad_mode)
-        main.wait_stream(side)
         dev = q_l.device
         out = torch.empty(B, H, Tl, D, dtype=out_dtype or q_l.dtype, device=dev)
-        kb = k_g[0].transpose(1, 2)  # rank 0's block as (B, H, Tl, D)
-        vb = v_g[0].transpose(1, 2)
+        kb = k_g[0, 0].permute(0, 2, 1, 3)  # block (chunk 0, rank 0) as (B, H, Tc, D)
+        vb = v_g[0, 0].permute(0, 2, 1, 3)
         K = idx.shape[-1]
         lib = _lib.load_library()
+        flags = _lib.WF_ATTN_MASK_NEGATIVE if self.pad_mode == "masked" else 0
         with torch.cuda.device(dev):
-            rc = lib.wf_sparse_attention_cyclic_kv(
-                q_l.data_ptr(), kb.data_ptr(), vb.data_ptr(), _lib.dtype_code(q_l.dtype), idx.data_ptr(),
-                B, H, Tl, T, D, K, _lib.strides(q_l), _lib.strides(kb), _lib.strides(vb), _lib.strides(idx),
-                float(self.scale), _lib.WF_ATTN_MASK_NEGATIVE if self.pad_mode == "masked" else 0,
-                out.data_ptr(), _lib.dtype_code(out.dtype), _lib.strides(out), self.tile, world,
-                k_g.stride(0), v_g.stride(0), None, _lib.stream_ptr(dev),
-            )
-        _lib.check(rc)
+            for c in list(range(1, C)) + [0]:
+                main.wait_event(landed[c] if c else landed[-1])
+                rows = slice(c * Tc, (c + 1) * Tc)
+                qc, ic, oc = q_l[:, :, rows], idx[:, rows], out[:, :, rows]
+                rc = lib.wf_sparse_attention_cyclic_kv_chunked(
+                    qc.data_ptr(), kb.data_ptr(), vb.data_ptr(), _lib.dtype_code(q_l.dtype), ic.data_ptr(),
+                    B, H, Tc, T, D, K, _lib.strides(qc), _lib.strides(kb), _lib.strides(vb), _lib.strides(ic),
+                    float(self.scale), flags, oc.data_ptr(), _lib.dtype_code(out.dtype), _lib.strides(oc),
+                    self.tile, world, Tc, k_g.stride(1), v_g.stride(1), None, _lib.stream_ptr(dev),
+                )
+                _lib.check(rc)
         return out, idx
 
     __call__ = forward
