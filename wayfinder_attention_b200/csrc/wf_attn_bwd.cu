@@ -309,7 +309,7 @@ __global__ void csr_fill_kernel(const AttnBwdParams p) {
 
 // --- key side ----------------------------------------------------------------
 template <typename TI, typename TG, int D, int E>
-__global__ void __launch_bounds__(256, 2) attn_bwd_key_kernel(const AttnBwdParams p) {
+__global__ void __launch_bounds__(128, 4) attn_bwd_key_kernel(const AttnBwdParams p) {
   using V16 = Vec16<TI>;
   constexpr int VEC = V16::N;
   constexpr int NV = E / VEC;
@@ -419,7 +419,7 @@ int launch_bwd_t(const AttnBwdParams& p, cudaStream_t stream) {
   csr_scan_kernel<<<p.B, 1024, 0, stream>>>(p);
   csr_fill_kernel<<<eg, 256, 0, stream>>>(p);
   const int64_t kwork = (int64_t)p.B * p.Tk * ngroups;
-  attn_bwd_key_kernel<TI, TG, D, E><<<(unsigned)((kwork + 7) / 8), 256, 0, stream>>>(p);
+  attn_bwd_key_kernel<TI, TG, D, E><<<(unsigned)((kwork + 3) / 4), 128, 0, stream>>>(p);
   return (int)cudaGetLastError();
 }
 
