@@ -103,9 +103,12 @@ WF_API size_t wf_causal_topk_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, 
  * allocator-less runtime, or code running where cudaMalloc is not permitted): the
  * retrieval scratch comes from a fixed 16 MiB device array built into this library,
  * which every GPU that loads the library keeps reserved until the process exits.
- * Same arguments and results as wf_causal_topk without the workspace; B*Tq is
- * limited to what fits in that array (2044 query rows for K <= 128; larger requests
- * return WF_ERR_UNSUPPORTED with the byte counts).  The first call on a device
+ * Same arguments and results as wf_causal_topk without the workspace.  A request
+ * fits when wf_causal_topk_workspace_bytes() for its sizes is at most 16 MiB:
+ * 2044 query rows (B*Tq) for K <= 128 with bf16/fp16 addresses; fp32 addresses also
+ * keep bf16 copies of the address rows there ((Tq + Tk) * R * 2 bytes per batch
+ * element), so fewer rows fit (e.g. 1792 at Tq = Tk, R = 32).  Larger requests
+ * return WF_ERR_UNSUPPORTED with the byte counts.  The first call on a device
  * looks up the array's device address, so make that first call before any stream
  * capture.  All calls share the one array: calls that overlap on the GPU (other
  * streams, other host threads) race on it and must be serialised by the caller.
@@ -305,6 +308,17 @@ WF_API int wf_sparse_attention_backward(const void* q, const void* k, const void
                                         uint64_t drop_seed, void* dq, void* dk, void* dv, int32_t grad_dtype, const int64_t* dq_strides,
                                         const int64_t* dk_strides, const int64_t* dv_strides, void* workspace,
                                         size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Test hook, no counterpart in the reference: makes the next tensor-core retrieval
+ * launch on this process exercise its timeout path without any fault.  CTA 1 of
+ * every CTA pair skips its arrive on the peer's barrier of bisection exchange
+ * `round` (0..7; negative turns the hook off), and the exchange waits give up after
+ * wait_limit_ns.  The waiting CTA then sets status bits 1 and 8 (wait site 256),
+ * drains its own copies and MMAs, frees its tensor memory and returns; the output
+ * of that launch is invalid.  Returns WF_OK.
+ */
+WF_API int wf_testing_withhold_pair_arrive(int32_t round, uint64_t wait_limit_ns);
 
 #ifdef __cplusplus
 }

@@ -45,6 +45,42 @@ def test_host_pipeline_matches_device_call(chunks, layout):
     assert torch.equal(out_h, ref_out.cpu())
 
 
+@pytest.mark.parametrize("shape", [(2, 4, 1000, 64, 64, 8), (1, 4, 2048, 64, 128, 8), (1, 2, 200, 32, 128, 4),
+                                   (1, 2, 512, 32, 16, 64)])
+def test_host_pipeline_first_call_on_poisoned_staging(shape, monkeypatch):
+    """The first call must not read staging rows before their upload lands.
+
+    Rows i < K-1 attend their pad rows (i + K + s + 1) % T, up to row 3K-2 and
+    wrapping when 3K-2 >= T, so they need later chunks than their own.  The device
+    staging buffers start as NaN (indices as garbage): any K/V row read before its
+    copy landed shows up as a NaN or a mismatch on the very first call.
+    """
+    from wayfinder_attention_b200 import HostFusedSparseAttention, fused_sparse_attention
+    from wayfinder_attention_b200 import host_pipeline
+
+    def poisoned(x, dev):
+        t = torch.empty_strided(tuple(x.shape), tuple(x.stride()), dtype=x.dtype, device=dev)
+        if t.dtype.is_floating_point:
+            t.fill_(float("nan"))
+        else:
+            t.fill_(-12345)
+        return t
+
+    monkeypatch.setattr(host_pipeline, "_device_like", poisoned)
+    B, H, T, D, K, chunks = shape
+    qa, ka, qkv = _inputs(B, H, T, D, 32, torch.bfloat16, 11)
+    q, k, v = (x.pin_memory().transpose(1, 2) for x in qkv)
+    scale = D ** -0.5
+    op = HostFusedSparseAttention(K, scale, chunks=chunks, device=0)
+    torch.cuda.synchronize()
+    out_h, idx_h = op(qa.pin_memory(), ka.pin_memory(), q, k, v)
+    torch.cuda.current_stream().synchronize()
+    ref_out, ref_idx = fused_sparse_attention(qa.cuda(), ka.cuda(), q.cuda(), k.cuda(), v.cuda(), K, scale)
+    assert torch.equal(idx_h, ref_idx.cpu())
+    assert not torch.isnan(out_h).any()
+    assert torch.equal(out_h, ref_out.cpu())
+
+
 def test_host_pipeline_against_oracle_and_outputs_given():
     from wayfinder_attention_b200 import host_fused_sparse_attention
 

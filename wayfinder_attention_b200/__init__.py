@@ -7,10 +7,12 @@ Public API (names and arguments of the reference's ``routing_attention``):
   op on pinned host tensors with upload, compute and download overlapped.
 
 The compute runs in ``libwayfinder_sm100.so`` (C ABI: ``include/wayfinder.h``);
-there is no CPU path.
+there is no CPU path.  Kernel faults that do not stop a kernel (an out-of-range
+index, a bounded wait that timed out) raise ``RuntimeError`` at the next call on
+the device, or at ``check_status()``, which waits for the device's queued work.
 """
 
-from ._lib import load_library
+from ._lib import check_status, load_library
 from .attention import (
     KeyVectorSparseAttention,
     LearnedAddressModule,
@@ -32,6 +34,7 @@ from .fused_sparse import (
 
 __all__ = [
     "load_library",
+    "check_status",
     "causal_topk",
     "causal_topk_available",
     "promote_compute_dtype",

@@ -8,12 +8,11 @@ is no fallback implementation, so a missing library raises immediately.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
 import torch
-
-import os
 
 # WF_LIB_PATH points at an alternative build of the same library (e.g. an instrumented one).
 LIB_PATH = Path(os.environ.get("WF_LIB_PATH") or Path(__file__).resolve().parent / "libwayfinder_sm100.so")
@@ -48,6 +47,8 @@ EXPORTED_SYMBOLS = (
     "wf_causal_topk_key_mask_workspace_bytes",
     "wf_sparse_attention_dropout",
     "wf_sparse_attention_cyclic_kv_chunked",
+    "wf_causal_topk_noalloc",
+    "wf_testing_withhold_pair_arrive",
 )
 
 _DTYPE_CODES = {
@@ -73,6 +74,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.wf_last_error.argtypes = []
     lib.wf_max_top_k.restype = ctypes.c_int
     lib.wf_max_top_k.argtypes = []
+    lib.wf_testing_withhold_pair_arrive.restype = ctypes.c_int
+    lib.wf_testing_withhold_pair_arrive.argtypes = [_i32, ctypes.c_uint64]
     lib.wf_causal_topk.restype = ctypes.c_int
     lib.wf_causal_topk.argtypes = [
         _vp, _vp, _i32, _i64, _i64, _i64, _i32, _i64p, _i64p, _i32, _i32, _i32, _i32, _i32, _vp,
@@ -196,3 +199,102 @@ def require_cuda(*tensors: torch.Tensor) -> torch.device:
         if t.device != dev:
             raise ValueError(f"tensors on different devices: {dev} vs {t.device}")
     return dev
+
+
+# ---------------------------------------------------------------- status word
+# Every kernel reports faults it can detect without stopping (an out-of-range
+# attention index: bit 0; a bounded wait that gave up: bit 1, plus a bit naming the
+# wait site from bit 4 up) by OR-ing bits into a caller-provided int32 status word.
+# A caller that passes none gets this per-device word: after each launch its value
+# is copied asynchronously into pinned host memory, and the next call on the device
+# (or ``check_status``) raises ``RuntimeError`` once that copy has landed.  No call
+# synchronises the host; ``check_status`` does, explicitly.
+
+STATUS_INDEX_OUT_OF_RANGE = 1
+STATUS_WAIT_TIMEOUT = 2
+
+
+class _DeviceStatus:
+    def __init__(self, dev: torch.device):
+        self.dev = dev
+        self.word = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.event = torch.cuda.Event()
+        self.pending = False
+
+    def poll(self, wait: bool = False) -> None:
+        if not self.pending:
+            return
+        if wait:
+            self.event.synchronize()
+        elif not self.event.query():
+            return
+        self.pending = False
+        bits = int(self.host[0])
+        if bits:
+            with torch.cuda.device(self.dev):
+                self.word.zero_()
+            raise RuntimeError(describe_status(bits))
+
+    def after_launch(self) -> None:
+        with torch.cuda.device(self.dev):
+            self.host.copy_(self.word, non_blocking=True)
+            self.event.record()
+        self.pending = True
+
+
+_status: dict[int, _DeviceStatus] = {}
+
+
+def describe_status(bits: int) -> str:
+    parts = []
+    if bits & STATUS_INDEX_OUT_OF_RANGE:
+        parts.append("an attention index was out of range (its output row is NaN)")
+    if bits & STATUS_WAIT_TIMEOUT:
+        parts.append(f"a kernel's bounded wait timed out (wait-site bits 0x{bits >> 4:x}); its results are invalid")
+    if not parts:
+        parts.append("unknown fault")
+    return f"wayfinder kernel status 0x{bits:x}: " + "; ".join(parts)
+
+
+def _device_status(dev: torch.device) -> _DeviceStatus:
+    i = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _status.get(i)
+    if st is None:
+        st = _status[i] = _DeviceStatus(torch.device("cuda", i))
+    return st
+
+
+def status_arg(dev: torch.device, user: torch.Tensor | None):
+    """Status pointer for a launch: the caller's word, else this device's internal one.
+
+    Raises the fault a previous call on ``dev`` left in the internal word, if its
+    read-back has landed.
+    """
+    if user is not None:
+        if user.dtype != torch.int32 or not user.is_cuda:
+            raise ValueError("status must be an int32 CUDA tensor")
+        return user.data_ptr()
+    st = _device_status(dev)
+    st.poll()
+    return st.word.data_ptr()
+
+
+def status_after(dev: torch.device, user: torch.Tensor | None) -> None:
+    """Queue the read-back of the internal status word after a launch that used it."""
+    if user is None:
+        _device_status(dev).after_launch()
+
+
+def check_status(device=None) -> None:
+    """Wait for the last calls on ``device`` (default: all used devices) and raise on any fault.
+
+    ``RuntimeError`` names the fault; the word is cleared, so later calls run normally.
+    """
+    if device is None:
+        targets = list(_status.values())
+    else:
+        d = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        targets = [_device_status(d)]
+    for st in targets:
+        st.poll(wait=True)

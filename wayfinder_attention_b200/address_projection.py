@@ -36,13 +36,15 @@ def address_projection(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor
     n_out = w.shape[0]
     out = torch.empty(x2.shape[0], n_out, dtype=x.dtype, device=dev)
     lib = _lib.load_library()
+    st = _lib.status_arg(dev, status)
     with torch.cuda.device(dev):
         rc = lib.wf_address_projection(
             x2.data_ptr(), _lib.dtype_code(x.dtype), x2.shape[0], x2.shape[1], x2.stride(0), w.data_ptr(),
             b.data_ptr() if b is not None else None, n_out, int(group), 1 if normalize else 0, out.data_ptr(),
-            out.stride(0), status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
+            out.stride(0), st, _lib.stream_ptr(dev),
         )
     _lib.check(rc)
+    _lib.status_after(dev, status)
     return out.view(*lead, n_out)
 
 

@@ -80,15 +80,17 @@ def _launch_topk(
     elif out.dtype != torch.int32 or not out.is_contiguous() or tuple(out.shape) != (B, Tq, k_eff):
         raise ValueError(f"out must be a contiguous int32 tensor of shape {(B, Tq, k_eff)}")
     ws = _lib.workspace(B, Tq, Tk, R, int(top_k), q.dtype, dev)
+    st = _lib.status_arg(dev, status)
     with torch.cuda.device(dev):
         rc = lib.wf_causal_topk(
             q.data_ptr(), k.data_ptr(), _lib.dtype_code(q.dtype), B, Tq, Tk, R,
             _lib.strides(q), _lib.strides(k), int(top_k), pad_mode_code(pad_mode),
             int(row_tile), int(row_stride), int(row_start), out.data_ptr(),
             ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
-            status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
+            st, _lib.stream_ptr(dev),
         )
     _lib.check(rc)
+    _lib.status_after(dev, status)
     return out
 
 
@@ -141,13 +143,15 @@ def _launch_topk_key_mask(q: torch.Tensor, k: torch.Tensor, top_k: int, key_mask
     out = torch.empty(B, T, k_eff, dtype=torch.int32, device=dev)
     n = lib.wf_causal_topk_key_mask_workspace_bytes(B, T, R, int(top_k), _lib.dtype_code(q.dtype))
     ws = torch.empty(max(n, 1), dtype=torch.uint8, device=dev)
+    st = _lib.status_arg(dev, status)
     with torch.cuda.device(dev):
         rc = lib.wf_causal_topk_key_mask(
             q.data_ptr(), k.data_ptr(), _lib.dtype_code(q.dtype), B, T, R, _lib.strides(q), _lib.strides(k),
             m.data_ptr(), _lib.strides(m), int(top_k), out.data_ptr(), ws.data_ptr(), ws.numel(),
-            status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
+            st, _lib.stream_ptr(dev),
         )
     _lib.check(rc)
+    _lib.status_after(dev, status)
     return out
 
 

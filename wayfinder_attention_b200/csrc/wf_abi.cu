@@ -135,6 +135,11 @@ const char* wf_last_error(void) { return g_err.c_str(); }
 
 int wf_max_top_k(void) { return wf::topk_max_k(); }
 
+int wf_testing_withhold_pair_arrive(int32_t round, uint64_t wait_limit_ns) {
+  wf::topk_tc_test_withhold(round, wait_limit_ns);
+  return ok();
+}
+
 size_t wf_causal_topk_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, int32_t R, int32_t top_k, int32_t dtype) {
   if (B <= 0 || Tq <= 0 || Tk <= 0 || top_k <= 0) return 0;
   const int64_t k_eff = top_k < Tk ? top_k : Tk;
@@ -450,9 +455,30 @@ int wf_fused_sparse_attention_host(const void* q_addr_h, const void* k_addr_h, i
   WF_CK(cudaEventRecord(e_idx, sm));
   WF_CK(cudaStreamWaitEvent(so, e_idx, 0));
   WF_CK(cudaMemcpyAsync(idx_h, d_idx, (size_t)(B * T) * k_eff * sizeof(int32_t), cudaMemcpyDeviceToHost, so));
-  for (int c = 0; c < chunks; ++c) {
+  // Chunk c's causal indices read K/V rows < e only, so it needs uploads 0..c.  With
+  // pad_mode=reference, rows i < K-1 also attend their pad rows (i + K + s + 1) % T,
+  // s < K, which reach row 3K-2 (and wrap to any row when 3K-2 >= T): a chunk holding
+  // such rows waits for the chunk of the highest pad row.  Chunks run in order of the
+  // upload they wait for, so the pad chunks go last and never hold up the others.
+  int need[64], order[64];
+  {
+    const int64_t pad_rows = pad_mode == WF_PAD_MASKED ? 0 : (int64_t)k_eff - 1;
+    const int64_t hi = 3 * (int64_t)top_k - 2 < T ? 3 * (int64_t)top_k - 2 : T - 1;
+    int c_hi = 0;
+    while (c_hi + 1 < chunks && T * (c_hi + 1) / chunks <= hi) ++c_hi;
+    int n = 0;
+    for (int c = 0; c < chunks; ++c) {
+      const int64_t a = T * c / chunks;
+      need[c] = (a < pad_rows && c_hi > c) ? c_hi : c;
+    }
+    for (int w = 0; w < chunks; ++w)
+      for (int c = 0; c < chunks; ++c)
+        if (need[c] == w) order[n++] = c;
+  }
+  for (int oi = 0; oi < chunks; ++oi) {
+    const int c = order[oi];
     const int64_t a = T * c / chunks, e = T * (c + 1) / chunks;
-    WF_CK(cudaStreamWaitEvent(sm, e_rows[c], 0));
+    WF_CK(cudaStreamWaitEvent(sm, e_rows[need[c]], 0));
     rc = wf_sparse_attention(static_cast<const char*>(d_q) + (size_t)(a * q_strides[2]) * esz, d_k, d_v, dtype,
                              d_idx + a * k_eff, B, H, e - a, T, D, k_eff, q_strides, k_strides, v_strides, is, scale,
                              pad_mode == WF_PAD_MASKED ? WF_ATTN_MASK_NEGATIVE : 0,

@@ -71,6 +71,9 @@ int launch_sparse_attention(const AttnParams& p, int dtype, int out_dtype, cudaS
 // Tk <= 65536, unit address stride, 16-byte aligned rows.
 bool topk_tc_supported(const TopkParams& p, int dtype);
 int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream);
+// Test hook: the next tensor-core top-K launch withholds CTA 1's arrive of bisection
+// exchange `round` (0..7; negative: off) and bounds those waits by wait_ns.
+void topk_tc_test_withhold(int round, uint64_t wait_ns);
 // Allocation-free retrieval: capacity of the library's built-in scratch array and
 // its device address on the current device (first call per device looks it up).
 size_t noalloc_scratch_capacity();

@@ -45,6 +45,7 @@
 #include "wf_select.cuh"
 #include "wf_sm100.cuh"
 
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -72,21 +73,6 @@ constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr float kEpsScale = 1.0f / 8192.0f;
 constexpr int kMaxDevices = 64;
 constexpr size_t kMaxSmem = 232448;
-#ifndef WF_TOPK_SKIP
-#define WF_TOPK_SKIP 0  // profiling builds only: bit mask of phases to skip
-#endif
-
-#ifndef WF_TOPK_PROF
-#define WF_TOPK_PROF 0  // profiling builds only: per-phase SM-cycle counters of the selection warps
-#endif
-#if WF_TOPK_PROF
-__device__ unsigned long long g_topk_prof[16];
-#define PROF_T(v) const long long v = clock64()
-#define PROF_ADD(slot, d) prof_acc[slot] += (unsigned long long)(d)
-#else
-#define PROF_T(v)
-#define PROF_ADD(slot, d)
-#endif
 
 struct TcParams {
   const void* q;
@@ -99,6 +85,11 @@ struct TcParams {
   uint64_t* ws;      // [B*Tq][kLists][KW] candidate composites (key << 32 | ~index)
   int32_t* ws_cnt;   // [B*Tq][kLists] candidate counts
   const int32_t* lim;  // optional [B][Tq] per-row key limits (see TopkParams)
+  // Test hook, set by wf_testing_withhold_pair_arrive (0 = off): CTA 1 of every pair
+  // skips its arrive on the peer's barrier of bisection exchange (withhold - 1), and
+  // the waits of the exchanges give up after xwait_ns, so CTA 0's wait runs out.
+  int withhold;
+  uint64_t xwait_ns;
   // fp32 addresses: the MMAs read bf16 copies; admitted keys are rescored from these
   const float* qf;
   const float* kf;
@@ -121,7 +112,7 @@ struct Layout {
   static constexpr size_t off_k = align_up(Q_BYTES, 1024);
   static constexpr size_t off_kmax = off_k + S * STAGE_STRIDE;
   static constexpr size_t off_bar = align_up(off_kmax + sizeof(float) * S, 8);
-  static constexpr size_t n_bar = 3 * S + 2 + kXRounds;  // full, mdone, done, qbar, kbar, xbar[rounds]
+  static constexpr size_t n_bar = 3 * S + 3 + kXRounds;  // full, mdone, done, qbar, kbar, xbar[rounds], drain
   static constexpr size_t off_misc = off_bar + 8 * n_bar;  // tmem base, kmax own, kmax peer, abort
   static constexpr size_t off_xslot = align_up(off_misc + 16, 16);  // [2 parities][kM rows][4] bisection exchange
   static constexpr size_t off_xpair = off_xslot + 4 * 2 * kM * 4;  // [2 parities][2 warps][kM][4] pair sums
@@ -146,8 +137,8 @@ __device__ __forceinline__ void pair_sync(int id) {
   asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
 }
 
-__device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity) {
-  return __all_sync(0xffffffffu, mbar_wait_cluster(bar, parity, kWaitLimitNs));
+__device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
+  return __all_sync(0xffffffffu, mbar_wait_cluster(bar, parity, limit_ns));
 }
 
 template <typename TI, int ROWB>
@@ -216,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // One single-use barrier per bisection exchange: a fast warp of the peer may post
   // step i+1 before a slow one has posted step i, so the steps cannot share phases.
   uint64_t* xbar = qbar + 2;
+  uint64_t* drain = xbar + kXRounds;  // the producer's last tcgen05.commit (nothing in flight at exit)
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(base + L::off_misc);
   uint32_t* kmax_own_s = tmem_base_s + 1;
   uint32_t* kmax_in_s = tmem_base_s + 2;
@@ -238,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int key_end = min(lrow ? lrow[nrows - 1] : g0 + nrows, p.Tk);
   const int nchunks = (key_end + kN - 1) / kN;
   const int n_own = nchunks > (int)rank ? (nchunks - (int)rank + 1) / 2 : 0;
-  const int n_work = (WF_TOPK_SKIP & 2) ? n_own : 2 * n_own;  // pass 1 + pass 2 items
+  const int n_work = 2 * n_own;  // pass 1 + pass 2 items
 
   if (warp == kEpiWarps && lane == 0) {
     for (int s = 0; s < S; ++s) {
@@ -249,6 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(qbar, 1);
     for (int i = 0; i < kXRounds; ++i) mbar_init(&xbar[i], 2 * kM);  // both warps of a quadrant post a row
     mbar_init(kbar, 2 * kM);
+    mbar_init(drain, 1);
     *kmax_own_s = 0u;
     fence_mbarrier_init();
   }
@@ -267,6 +260,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kEpiWarps) {
     // ============================================================ producer
+    // pend[s]: item whose key load into stage s was issued and not yet waited for (-1: none)
+    int pend[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) pend[s] = s < n_work ? s : -1;
     if (lane == 0) {
       prefetch_tmap(&qmap);
       prefetch_tmap(&kmap);
@@ -278,12 +275,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     ok = warp_wait(qbar, 0);
+    const bool q_landed = ok;
     if (!ok) why |= 4;
     uint32_t kbits = 0;
     for (int w = 0; w < n_work && ok; ++w) {
       const int s = w % S;
       unsigned char* stage = ks + s * L::STAGE_STRIDE;
       if (!warp_wait(&full[s], (uint32_t)(w / S) & 1u)) { ok = false; why |= 8; break; }
+      pend[s] = -1;
       // accumulator (w & 1) was last read by item w-2
       if (w >= 2 && !warp_wait(&done[(w - 2) % S], (uint32_t)((w - 2) / S) & 1u)) { ok = false; why |= 16; break; }
       tc_fence_after();
@@ -324,9 +323,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&full[s1], (uint32_t)L::STAGE_BYTES);
           tma_load_3d(ks + s1 * L::STAGE_STRIDE, &kmap, &full[s1], 0, chunk_of(wn) * kN, b);
         }
+        pend[s1] = wn;
       }
       __syncwarp();
     }
+    // Drain before the CTA may exit: every MMA this thread issued has completed when
+    // the commit below arrives, and every key or q load that no wait consumed has
+    // landed (all waits bounded; on a timeout the status word already says so).
+    if (lane == 0) {
+      mma_commit(drain);
+      mbar_wait(drain, 0, kWaitLimitNs);
+      if (!q_landed) mbar_wait(qbar, 0, kWaitLimitNs);
+#pragma unroll
+      for (int s = 0; s < S; ++s)
+        if (pend[s] >= 0) mbar_wait(&full[s], (uint32_t)(pend[s] / S) & 1u, kWaitLimitNs);
+    }
+    __syncwarp();
   } else {
     // ============================================================ selection
     // Two warps per TMEM lane quadrant: warp w owns rows 32*(w%4) .. +31 and the
@@ -368,10 +380,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     ok = warp_wait(qbar, 0);
     if (!ok) why |= 64;
 
-#if WF_TOPK_PROF
-    unsigned long long prof_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#endif
-    PROF_T(tp1s);
     // ---------------- pass 1: group maxima of tensor-core scores (this warp's slices)
     for (int w = 0; w < n_own && ok; ++w) {
       const int s = w % S;
@@ -418,8 +426,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     pair_sync(pair_bar);
     tc_fence_after();
 
-    PROF_T(tp1e);
-    PROF_ADD(0, tp1e - tp1s);
     // ---------------- lower bound on the K-th best score from the pair's 512 group maxima
     // Both CTAs bisect the same value range over the union of their maxima: each
     // step counts its own maxima >= mid, swaps the count with the peer thread of the
@@ -468,8 +474,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       st_peer_u32(peer_slot, x[0]);
       st_peer_u32(peer_slot + 4, x[1]);
       st_peer_u32(peer_slot + 8, x[2]);
-      mbar_arrive_peer(map_peer(&xbar[round], peer));
-      if (!warp_wait_cluster(&xbar[round], 0)) { ok = false; why |= 256; }
+      if (!(p.withhold == round + 1 && rank == 1)) mbar_arrive_peer(map_peer(&xbar[round], peer));
+      if (!warp_wait_cluster(&xbar[round], 0, p.xwait_ns)) { ok = false; why |= 256; }
       got[0] = slot[0];
       got[1] = slot[1];
       got[2] = slot[2];
@@ -515,8 +521,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float eps = (F32 ? 1.0f / 64.0f : kEpsScale) * qabs * kpair;
     float lim = theta > -INFINITY ? theta - eps : -INFINITY;
 
-    PROF_T(tbe);
-    PROF_ADD(1, tbe - tp1e);
     // ---------------- pass 2: admit, rescore exactly, keep candidates in the workspace
     uint32_t* queue = queues + warp * kQcap;
     const int64_t row0 = (int64_t)b * p.Tq + l0 + 32 * qd;  // first row of this quadrant
@@ -548,15 +552,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = n_own; w < n_work; ++w) {
       const int s = w % S;
       const uint32_t ph = (uint32_t)(w / S) & 1u;
-      PROF_T(tw0);
       if (alive && (!warp_wait(&mdone[s], ph) || !warp_wait(&full[s], ph))) {
         alive = false;
         ok = false;
         why |= 512;
       }
       tc_fence_after();
-      PROF_T(tw1);
-      PROF_ADD(2, tw1 - tw0);
       const int c = chunk_of(w);
       const unsigned char* stage = ks + s * L::STAGE_STRIDE;
       const uint32_t acc = tmem_base + lane_base + (uint32_t)((w & 1) * kN);
@@ -578,8 +579,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           masks[i] = m;
         }
       }
-      PROF_T(tw2);
-      PROF_ADD(3, tw2 - tw1);
       const int np = __popc(masks[0]) + __popc(masks[1]);
       // A list that this chunk could overflow is compacted to its exact top-K first
       // (queued entries written out beforehand); that also raises the row's threshold.
@@ -634,24 +633,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       qsize += total;
-      PROF_T(tw3);
-      PROF_ADD(4, tw3 - tw2);
       flush(stage, c);  // the stage is about to be released
-      PROF_T(tw4);
-      PROF_ADD(5, tw4 - tw3);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&done[s]);
     }
     if (row_ok) p.ws_cnt[((row0 + lane) * 2 + rank) * 2 + hf] = cnt;
-#if WF_TOPK_PROF
-    PROF_T(tend);
-    PROF_ADD(6, tend - tbe);
-    PROF_ADD(7, tend - tp1s);
-    if (lane == 0)
-      for (int i = 0; i < 8; ++i) atomicAdd(&g_topk_prof[i], prof_acc[i]);
-    if (lane == 0) atomicAdd(&g_topk_prof[8], 1ull);
-#endif
   }
   if (!ok && p.status) atomicOr(p.status, 2 | (int)why);
 
@@ -766,19 +753,11 @@ __global__ void __launch_bounds__(kFinWarps * 32, 2) topk_finalize_kernel(const 
   else finalize_row<E2, SE>(p, row, nl, lane, skey[warp], sidx[warp]);
 }
 
-#if WF_TOPK_PROF
-}  // namespace
-}  // namespace wf
-extern "C" __attribute__((visibility("default"))) int wf_debug_topk_prof(unsigned long long* out16) {
-  cudaError_t e = cudaMemcpyFromSymbol(out16, wf::g_topk_prof, sizeof(unsigned long long) * 16);
-  unsigned long long z[16] = {};
-  if (e == cudaSuccess) e = cudaMemcpyToSymbol(wf::g_topk_prof, z, sizeof(z));
-  return (int)e;
-}
-namespace wf {
-namespace {
-#endif
 // ---------------------------------------------------------------- host side
+// Test hook (wf_testing_withhold_pair_arrive): consumed by the next launch.
+std::atomic<int> g_test_withhold{0};
+std::atomic<uint64_t> g_test_xwait_ns{kWaitLimitNs};
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -915,6 +894,8 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
     t.status = p.status;
     t.ws = ws;
     t.ws_cnt = ws_cnt;
+    t.withhold = g_test_withhold.exchange(0);
+    t.xwait_ns = t.withhold ? g_test_xwait_ns.load() : kWaitLimitNs;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * ((p.Tq + kM - 1) / kM), nb);
@@ -987,6 +968,11 @@ size_t topk_tc_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, int R, int K, 
   const int64_t bpp = batch_per_pass(B, Tq);
   const size_t lists = (size_t)bpp * Tq * ws_bytes_per_row(K);
   return dtype == kF32 ? lists + shadow_bytes_pass(bpp, Tq, Tk, R) : lists;
+}
+
+void topk_tc_test_withhold(int round, uint64_t wait_ns) {
+  g_test_xwait_ns.store(wait_ns);
+  g_test_withhold.store(round >= 0 && round < kXRounds ? round + 1 : 0);
 }
 
 int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream) {

@@ -84,10 +84,8 @@ def _launch_attention(
         # softmax over an empty set: the reference's sum over zero rows is 0
         return out.zero_()
     q, k, v = _attn_operand(q), _attn_operand(k), _attn_operand(v)
-    if status is not None and (status.dtype != torch.int32 or not status.is_cuda):
-        raise ValueError("status must be an int32 CUDA tensor")
     flags = _lib.WF_ATTN_MASK_NEGATIVE if mask_negative else 0
-    st = status.data_ptr() if status is not None else None
+    st = _lib.status_arg(dev, status)
     with torch.cuda.device(dev):
         if drop_rate > 0.0:
             rc = lib.wf_sparse_attention_dropout(
@@ -105,6 +103,7 @@ def _launch_attention(
                 st, _lib.stream_ptr(dev),
             )
     _lib.check(rc)
+    _lib.status_after(dev, status)
     return out
 
 
@@ -123,6 +122,7 @@ def _launch_attention_backward(q, k, v, indices, dout, scale, mask_negative, sta
     dv = torch.empty_like(v)
     n = lib.wf_sparse_attention_backward_workspace_bytes(B, H, Tq, Tk, K)
     ws = torch.empty(max(n, 1), dtype=torch.uint8, device=dev)
+    st = _lib.status_arg(dev, status)
     with torch.cuda.device(dev):
         rc = lib.wf_sparse_attention_backward(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.dtype_code(q.dtype), indices.data_ptr(),
@@ -130,9 +130,10 @@ def _launch_attention_backward(q, k, v, indices, dout, scale, mask_negative, sta
             dout.data_ptr(), _lib.strides(dout), float(scale), _lib.WF_ATTN_MASK_NEGATIVE if mask_negative else 0,
             float(drop_rate), int(drop_seed), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _lib.dtype_code(q.dtype), _lib.strides(dq),
             _lib.strides(dk), _lib.strides(dv), ws.data_ptr(), ws.numel(),
-            status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
+            st, _lib.stream_ptr(dev),
         )
     _lib.check(rc)
+    _lib.status_after(dev, status)
     return dq, dk, dv
 
 
@@ -257,8 +258,6 @@ def fused_sparse_attention(
     H, D = q.shape[1], q.shape[3]
     idx = torch.empty(B, T, k_eff, dtype=torch.int32, device=dev)
     out = torch.empty(B, H, T, D, dtype=out_dtype or q.dtype, device=dev)
-    if status is not None and (status.dtype != torch.int32 or not status.is_cuda):
-        raise ValueError("status must be an int32 CUDA tensor")
     if key_mask is not None:
         # padded keys are never retrieved; slots a row cannot fill are masked out of the softmax
         from .causal_topk import _launch_topk_key_mask
@@ -267,6 +266,7 @@ def fused_sparse_attention(
         out = _launch_attention(q, k, v, idx, scale, mask_negative=True, out_dtype=out_dtype, status=status)
         return out, idx
     ws = _lib.workspace(B, T, T, R, int(top_k), qa.dtype, dev)
+    st = _lib.status_arg(dev, status)
     with torch.cuda.device(dev):
         rc = lib.wf_fused_sparse_attention(
             qa.data_ptr(), ka.data_ptr(), _lib.dtype_code(qa.dtype), R, _lib.strides(qa), _lib.strides(ka),
@@ -274,9 +274,10 @@ def fused_sparse_attention(
             _lib.strides(q), _lib.strides(k), _lib.strides(v), int(top_k), float(scale),
             pad_mode_code(pad_mode), 0, 1, 0, idx.data_ptr(), out.data_ptr(), _lib.dtype_code(out.dtype),
             _lib.strides(out), ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
-            status.data_ptr() if status is not None else None, _lib.stream_ptr(dev),
+            st, _lib.stream_ptr(dev),
         )
     _lib.check(rc)
+    _lib.status_after(dev, status)
     return out, idx
 
 

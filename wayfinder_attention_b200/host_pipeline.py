@@ -107,6 +107,7 @@ class HostFusedSparseAttention:
             self._s_out = torch.cuda.Stream(device=dev)
         ws = self._ws
         lib = _lib.load_library()
+        st = _lib.status_arg(dev, None)
         with torch.cuda.device(dev):
             rc = lib.wf_fused_sparse_attention_host(
                 qa_h.data_ptr(), ka_h.data_ptr(), _lib.dtype_code(qa_h.dtype), R,
@@ -116,10 +117,11 @@ class HostFusedSparseAttention:
                 _lib.dtype_code(out.dtype), _lib.strides(out),
                 d["qa"].data_ptr(), d["ka"].data_ptr(), d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(),
                 d["idx"].data_ptr(), d["out"].data_ptr(), ws.data_ptr() if ws is not None else None,
-                ws.numel() if ws is not None else 0, None, _lib.stream_ptr(dev),
+                ws.numel() if ws is not None else 0, st, _lib.stream_ptr(dev),
                 self._s_in.cuda_stream, self._s_out.cuda_stream,
             )
         _lib.check(rc)
+        _lib.status_after(dev, None)
         return out, idx_out
 
     forward = __call__

@@ -165,6 +165,9 @@ class SequenceShardedAttention:
             self._kg = torch.empty(shape, dtype=k_l.dtype, device=k_l.device)
             self._vg = torch.empty(shape, dtype=v_l.dtype, device=v_l.device)
         k_g, v_g = self._kg, self._vg
+        # The key addresses (small) go first: collectives of one process group run in
+        # issue order, so issued after the K/V chunks the retrieval would wait for them.
+        k_addr = gather_sequence(k_addr_l, self.tile, self.group)  # reordered to global order
         side.wait_stream(main)  # the previous call's attention has finished with the buffers
         landed = []
         with torch.cuda.stream(side):
@@ -175,7 +178,6 @@ class SequenceShardedAttention:
                 ev = torch.cuda.Event()
                 ev.record(side)
                 landed.append(ev)
-        k_addr = gather_sequence(k_addr_l, self.tile, self.group)  # small: reordered to global order
         idx = sharded_causal_topk(q_addr_l, k_addr, self.top_k, world, rank, self.tile, self.pad_mode)
         dev = q_l.device
         out = torch.empty(B, H, Tl, D, dtype=out_dtype or q_l.dtype, device=dev)
@@ -184,6 +186,7 @@ class SequenceShardedAttention:
         K = idx.shape[-1]
         lib = _lib.load_library()
         flags = _lib.WF_ATTN_MASK_NEGATIVE if self.pad_mode == "masked" else 0
+        st = _lib.status_arg(dev, None)
         with torch.cuda.device(dev):
             for c in list(range(1, C)) + [0]:
                 main.wait_event(landed[c] if c else landed[-1])
@@ -193,9 +196,10 @@ class SequenceShardedAttention:
                     qc.data_ptr(), kb.data_ptr(), vb.data_ptr(), _lib.dtype_code(q_l.dtype), ic.data_ptr(),
                     B, H, Tc, T, D, K, _lib.strides(qc), _lib.strides(kb), _lib.strides(vb), _lib.strides(ic),
                     float(self.scale), flags, oc.data_ptr(), _lib.dtype_code(out.dtype), _lib.strides(oc),
-                    self.tile, world, Tc, k_g.stride(1), v_g.stride(1), None, _lib.stream_ptr(dev),
+                    self.tile, world, Tc, k_g.stride(1), v_g.stride(1), st, _lib.stream_ptr(dev),
                 )
                 _lib.check(rc)
+        _lib.status_after(dev, None)
         return out, idx
 
     __call__ = forward
