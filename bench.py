@@ -25,7 +25,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -42,9 +41,10 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 E2E_CHUNKS = 4  # query-row chunks of the host pipeline
 L2_FLUSH_BYTES = 256 << 20
 METRIC = "fused top-K+sparse-attn fwd queries/s @T=16K,K=128"
-# dram__bytes_read.sum + dram__bytes_write.sum of one sparse-attention launch, from the
-# ncu capture summarised in profiles/sparse_attention_cfg2.md (58.0 MB + 4.4 MB).
+# dram__bytes_read.sum + dram__bytes_write.sum of one sparse-attention launch: constants
+# from the named ncu captures (not measured in this run).
 ATTN_DRAM_BYTES = {"cfg2": 62.3e6}
+ATTN_DRAM_SOURCE = {"cfg2": "profiles/sparse_attention_cfg2.md"}
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -83,8 +83,8 @@ class ClockSampler:
     """Samples SM clock and clock-event reasons during the timed region.
 
     Reads NVML (read-only queries) every ~2 ms from a background thread, so even a
-    timed region of a few tens of milliseconds gets samples; falls back to an
-    `nvidia-smi` poll if NVML is unavailable.
+    timed region of a few tens of milliseconds gets samples; without NVML the
+    summary reports no samples.
     """
 
     REASONS = {
@@ -217,6 +217,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-dense", action="store_true")
     ap.add_argument("--no-decoder", action="store_true", help="skip the whole-decoder prefill measurements")
+    ap.add_argument("--no-extra-configs", action="store_true",
+                    help="skip the cfg4 / cfg5 measurements (and the sequence-sharded cfg4 run at N > 1)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     claim_stdout()
@@ -297,6 +299,7 @@ def main() -> None:
     torch.cuda.synchronize()
     topk_tot = sum(e[0].elapsed_time(e[1]) for e in kev)
     attn_tot = sum(e[1].elapsed_time(e[2]) for e in kev)
+    ceiling_gbs = gather_ceiling(x, idx, args.steps, flush, stream)
     t = torch.tensor([total_ms, topk_tot, attn_tot], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -352,9 +355,39 @@ def main() -> None:
             dist.all_reduce(t_, op=dist.ReduceOp.MAX)
         return t_.item() / args.steps
 
+    # The copies alone, as the pipelined call issues them (uploads on one stream,
+    # downloads on another, both directions at once), on every rank at the same time:
+    # the host-link ceiling of the e2e number.
+    s_up, s_dn = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    dn_src = torch.empty(d2h, dtype=torch.uint8, device=dev)
+    dn_dst = torch.empty(d2h, dtype=torch.uint8).pin_memory()
+
+    def copies_only():
+        s_up.wait_stream(stream)
+        s_dn.wait_stream(stream)
+        with torch.cuda.stream(s_up):
+            for k_ in pin:
+                dbuf[k_].copy_(pin[k_], non_blocking=True)
+        with torch.cuda.stream(s_dn):
+            dn_dst.copy_(dn_src, non_blocking=True)
+        stream.wait_stream(s_up)
+        stream.wait_stream(s_dn)
+
     e2e_serial_ms = time_e2e(e2e_serial)
     e2e_ms_step = time_e2e(e2e_pipelined)
+    copy_ms = time_e2e(copies_only)
     e2e_value = queries / (e2e_ms_step / 1e3)
+
+    # the one data path with a collective: cfg4's long sequence over all ranks, and the
+    # same call on one GPU (rank 0, the others wait) for the strong-scaling efficiency
+    seq = None
+    if world > 1 and not args.no_extra_configs:
+        seq = sequence_sharded_measure(CONFIGS["cfg4"], rank, world, dev, max(3, args.steps // 4), 3)
+        if rank == 0:
+            one = config_measurement("cfg4", dev, flush, max(3, args.steps // 4))
+            seq["single_gpu_ms"] = one["ms"]
+            seq["strong_scaling_efficiency"] = one["ms"] / (world * seq["ms"])
+        dist.barrier()
 
     result = None
     if rank == 0:
@@ -366,6 +399,8 @@ def main() -> None:
         hbm = float(peaks["hbm_gbs"])
         tens = float(peaks["bf16_tflops"]) * 1e12
         roof_s = max(w.score_flops() / tens, gathered / (hbm * 1e9))
+        roof_l2_s = max(w.score_flops() / tens, gathered / (ceiling_gbs * 1e9))
+        dram = ATTN_DRAM_BYTES.get(w.name)
         result = {
             "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -379,18 +414,36 @@ def main() -> None:
             "query_heads_per_s": value * w.H,
             "kernels_ms": {"causal_topk": topk_ms_launch, "sparse_attention": attn_ms_launch,
                            "note": "each kernel timed alone, same launches as the step"},
-            "roofline": {"kernel": "sparse_attention", "bound": "hbm", "achieved": achieved_gbs, "peak": hbm,
-                         "unit": "GB/s", "frac": achieved_gbs / hbm,
-                         "traffic": ATTN_DRAM_BYTES.get(w.name),
-                         "peak_kind": peak_kind,
-                         "note": "achieved = gathered K/V bytes (2*B*H*T*K*D*2) / kernel time; K/V fit in L2"},
-            "path_roofline": {"roofline_ms": roof_s * 1e3, "frac": roof_s * 1e3 / ms_per_step,
+            # cfg2's K/V (33.5 MB) stay in the 126 MB L2, so the gathers are served from L2:
+            # the binding resource is the L2 -> SM load stream, whose ceiling for this
+            # access pattern is measured in this run by wf_gather_rows_bench (same loads,
+            # same indices, no math).  The HBM view uses the DRAM bytes of a named capture.
+            "roofline": {"kernel": "sparse_attention", "bound": "l2", "achieved": achieved_gbs,
+                         "peak": ceiling_gbs, "unit": "GB/s", "frac": achieved_gbs / ceiling_gbs,
+                         "peak_kind": "measured in this run (wf_gather_rows_bench: the kernel's K/V row loads "
+                                      "over the same indices, nothing computed)",
+                         "traffic": dram,
+                         "traffic_source": (ATTN_DRAM_SOURCE.get(w.name, "") +
+                                            " (constant from that ncu capture, not measured in this run)"),
+                         "hbm": {"achieved": (dram / (attn_ms_launch / 1e3) / 1e9) if dram else None, "peak": hbm,
+                                 "frac": (dram / (attn_ms_launch / 1e3) / 1e9 / hbm) if dram else None,
+                                 "peak_kind": peak_kind},
+                         "note": "achieved = gathered K/V bytes (2*B*H*T*K*D*2) / kernel time"},
+            "path_roofline": {"roofline_ms": roof_l2_s * 1e3, "frac": roof_l2_s * 1e3 / ms_per_step,
                               "score_tflops_achieved": w.score_flops() / (topk_ms_launch / 1e3) / 1e12,
-                              "definition": "max(score FLOPs / bf16 peak, gathered bytes / HBM peak) / latency"},
+                              "definition": "max(score FLOPs / bf16 peak, gathered bytes / measured gather "
+                                            "ceiling) / latency",
+                              "north_star_form": {"roofline_ms": roof_s * 1e3, "frac": roof_s * 1e3 / ms_per_step,
+                                                  "definition": "max(score FLOPs / bf16 peak, gathered bytes / "
+                                                                "HBM peak); above 1 because the gathers hit L2"}},
             "peak_mb": peak_mb,
             "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms_step, "api": "HostFusedSparseAttention (copies overlapped, "
-                    f"{E2E_CHUNKS} row chunks)", "serial_ms_per_step": e2e_serial_ms},
+                    f"{E2E_CHUNKS} row chunks)", "serial_ms_per_step": e2e_serial_ms,
+                    "copies_only_ms_per_step": copy_ms,
+                    "host_link_gbs_per_rank": (h2d + d2h) / (copy_ms / 1e3) / 1e9,
+                    "frac_of_copy_ceiling": copy_ms / e2e_ms_step,
+                    "note": "copies_only: the same uploads and downloads on every rank at once, no kernels"},
             "gpu_launches": 3 * args.steps,  # per step: retrieval, finalisation, attention
             "clocks": clk.summary(),
         }
@@ -405,6 +458,12 @@ def main() -> None:
                 "cfg3_B8_T4096": decoder_forward(8, 4096, flush, 5, dev),
                 "published_rtx5090_ms": {"wayfinder_T16384": 38.35, "dense_flash_T16384": 84.33},
             }
+        if seq is not None:
+            result["cfg4_sequence_sharded"] = seq
+        if world == 1 and not args.no_extra_configs:
+            # configurations whose K/V outgrow the 126 MB L2 (cfg4: 1.07 GB; cfg5: 2.1 GB per call)
+            result["cfg4_single_gpu"] = config_measurement("cfg4", dev, flush, max(3, args.steps // 4))
+            result["cfg5_k128"] = config_measurement("cfg5", dev, flush, max(3, args.steps // 4))
         if world == 1 and not args.no_cpu_baseline:
             secs, n = time_cpu_oracle(w, host, args.cpu_baseline_rows)
             result["cpu_baseline"] = {
@@ -420,46 +479,79 @@ def main() -> None:
         emit(result)
 
 
-def run_sequence_sharded(args, w: Workload, rank: int, world: int, dev) -> None:
-    """cfg4: one T=65536 sequence, query-row blocks over ranks, address and K/V all-gathers (strong scaling)."""
+def sequence_sharded_measure(w: Workload, rank: int, world: int, dev, steps: int, warmup: int) -> dict:
+    """cfg4 on ``world`` ranks: query-row blocks cyclic over ranks, k_addr and K/V all-gathered.
+
+    Returns the per-step time (max over ranks, CUDA events, L2 flushed before each
+    step) and, for the limiter, the parts timed alone: the K/V all-gathers, the
+    rank's retrieval and its attention over landed K/V.
+    """
     import torch.distributed as dist
 
-    from wayfinder_attention_b200.sharding import SequenceShardedAttention, local_rows
+    from wayfinder_attention_b200.sharding import (SequenceShardedAttention, _all_gather_rows, chunked_kv_attention,
+                                                   gather_sequence, local_rows, sharded_causal_topk)
 
     tile = 256
     if w.T % (world * tile):
         raise SystemExit(f"T={w.T} is not a multiple of world*tile={world * tile}")
-    g = torch.Generator(device=dev).manual_seed(45)  # identical full inputs on every rank
-    qa = (torch.randn(w.B, w.T, w.R, generator=g, device=dev) / 32 ** 0.5).to(w.dtype)
-    ka = (torch.randn(w.B, w.T, w.R, generator=g, device=dev) / 32 ** 0.5).to(w.dtype)
-    qkv = [torch.randn(w.B, w.T, w.H, w.D, generator=g, device=dev).to(w.dtype) for _ in range(3)]
+    full = device_inputs(w, dev)  # identical on every rank (same seed)
     rows = torch.from_numpy(local_rows(w.T, world, rank, tile)).to(dev)
-    qa_l, ka_l = qa[:, rows].contiguous(), ka[:, rows].contiguous()
-    q_l, k_l, v_l = (t[:, rows].contiguous().transpose(1, 2) for t in qkv)
-    del qa, ka, qkv
+    qa_l, ka_l = full["q_addr"][:, rows].contiguous(), full["k_addr"][:, rows].contiguous()
+    q_l, k_l, v_l = (full[n].transpose(1, 2)[:, rows].contiguous().transpose(1, 2) for n in ("q", "k", "v"))
+    del full
+    torch.cuda.empty_cache()
     op = SequenceShardedAttention(w.K, w.D ** -0.5, tile=tile)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    for _ in range(args.warmup):
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(warmup):
         flush.zero_()
         op(qa_l, ka_l, q_l, k_l, v_l)
     torch.cuda.synchronize()
-    dist.barrier()
-    stream = torch.cuda.current_stream(dev)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    torch.cuda.synchronize()
-    dist.barrier()
-    with ClockSampler(int(os.environ.get("LOCAL_RANK", 0))) as clk:
-        for i in range(args.steps):
+
+    def timed(fn):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        torch.cuda.synchronize()
+        dist.barrier()
+        for a, b in ev:
             flush.zero_()
             dist.barrier()  # all ranks enter the step together, outside the timed events
-            ev[i][0].record(stream)
-            op(qa_l, ka_l, q_l, k_l, v_l)
-            ev[i][1].record(stream)
+            a.record(stream)
+            fn()
+            b.record(stream)
         torch.cuda.synchronize()
-    dist.barrier()
-    tot = torch.tensor([sum(a.elapsed_time(b) for a, b in ev)], dtype=torch.float64, device=dev)
-    dist.all_reduce(tot, op=dist.ReduceOp.MAX)
-    ms = tot.item() / args.steps
+        tot = torch.tensor([sum(a.elapsed_time(b) for a, b in ev)], dtype=torch.float64, device=dev)
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+        return tot.item() / steps
+
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", 0))) as clk:
+        ms = timed(lambda: op(qa_l, ka_l, q_l, k_l, v_l))
+    # the parts alone (same buffers and chunking as the op)
+    k_g, v_g = op._kg, op._vg
+    C, Tc = k_g.shape[0], k_g.shape[3]
+    kt, vt = k_l.transpose(1, 2), v_l.transpose(1, 2)
+
+    def gathers():
+        for c in range(C):
+            _all_gather_rows(kt[:, c * Tc:(c + 1) * Tc], world, None, k_g[c])
+            _all_gather_rows(vt[:, c * Tc:(c + 1) * Tc], world, None, v_g[c])
+
+    k_addr = gather_sequence(ka_l, tile)
+    idx = sharded_causal_topk(qa_l, k_addr, w.K, world, rank, tile)
+    gather_ms = timed(gathers)
+    retrieval_ms = timed(lambda: sharded_causal_topk(qa_l, gather_sequence(ka_l, tile), w.K, world, rank, tile))
+    attention_ms = timed(lambda: chunked_kv_attention(q_l, idx, k_g, v_g, w.D ** -0.5, tile))
+    kv_recv = 2.0 * (world - 1) / world * w.B * w.T * w.H * w.D * q_l.element_size()
+    return {"ms": ms, "n_gpus": world, "chunks": C, "clocks": clk.summary(),
+            "parts_ms": {"kv_allgather": gather_ms, "retrieval_with_addr_gather": retrieval_ms,
+                         "attention": attention_ms},
+            "kv_bytes_received_per_rank": kv_recv,
+            "kv_allgather_gbs_per_rank": kv_recv / (gather_ms / 1e3) / 1e9}
+
+
+def run_sequence_sharded(args, w: Workload, rank: int, world: int, dev) -> None:
+    """cfg4 as the workload: one T=65536 sequence over the ranks (strong scaling)."""
+    m = sequence_sharded_measure(w, rank, world, dev, args.steps, args.warmup)
+    ms = m["ms"]
     if rank == 0:
         peaks, peak_kind = load_peaks()
         roof_ms = 1e3 * max(w.score_flops() / (float(peaks["bf16_tflops"]) * 1e12),
@@ -469,13 +561,102 @@ def run_sequence_sharded(args, w: Workload, rank: int, world: int, dev) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, generated on device)",
             "config": {"workload": w.name, "B": w.B, "H": w.H, "T": w.T, "D": w.D, "d_A": w.R, "K": w.K,
-                       "parallelism": f"query-row blocks of {tile} cyclic over {world} ranks; "
+                       "parallelism": f"query-row blocks of 256 cyclic over {world} ranks; "
                                       "k_addr and K/V all-gathered with NCCL",
                        "l2": "flushed before every timed step"},
             "path_roofline": {"roofline_ms_per_gpu": roof_ms, "frac": roof_ms / ms, "peak_kind": peak_kind},
-            "gpu_launches": 3 * args.steps,  # per step: retrieval, finalisation, attention
-            "clocks": clk.summary(),
+            "parts_ms": m["parts_ms"],
+            "gpu_launches": (2 + m["chunks"]) * args.steps,  # per step: retrieval, finalisation, attention chunks
+            "clocks": m["clocks"],
         })
+
+
+def device_inputs(w: Workload, dev, seed: int = 45) -> dict:
+    """Seeded inputs of workload ``w`` drawn on the device (large configs: no host round trip)."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    if w.clustered:
+        centres = torch.randn(64, w.R, generator=g, device=dev) / 32 ** 0.5
+        pick = lambda: centres[torch.randint(0, 64, (w.B, w.T), generator=g, device=dev)]  # noqa: E731
+        qa = pick() + 0.05 * torch.randn(w.B, w.T, w.R, generator=g, device=dev)
+        ka = pick() + 0.05 * torch.randn(w.B, w.T, w.R, generator=g, device=dev)
+    else:
+        qa = torch.randn(w.B, w.T, w.R, generator=g, device=dev) / 32 ** 0.5
+        ka = torch.randn(w.B, w.T, w.R, generator=g, device=dev) / 32 ** 0.5
+    out = {"q_addr": qa.to(w.dtype), "k_addr": ka.to(w.dtype)}
+    for n in ("q", "k", "v"):
+        out[n] = torch.randn(w.B, w.T, w.H, w.D, generator=g, device=dev).to(w.dtype).transpose(1, 2)
+    return out
+
+
+def time_events(fn, steps: int, flush: torch.Tensor, stream) -> float:
+    """Mean ms of ``fn`` over ``steps`` launches, L2 flushed before each, CUDA events on ``stream``."""
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in ev:
+        flush.zero_()
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in ev) / steps
+
+
+def gather_ceiling(x: dict, idx: torch.Tensor, steps: int, flush: torch.Tensor, stream) -> float:
+    """GB/s of wf_gather_rows_bench: the attention kernel's K/V row loads over the same indices, no math."""
+    from wayfinder_attention_b200 import _lib
+
+    lib = _lib.load_library()
+    k, v = x["k"], x["v"]  # (B, H, T, D) views of (B, T, H, D) memory: one token's heads are contiguous
+    B, H, T, D = k.shape
+    esz = k.element_size()
+    sink = torch.empty(B * T, dtype=torch.int32, device=k.device)
+    K = idx.shape[-1]
+
+    def run():
+        for b in range(B):
+            rc = lib.wf_gather_rows_bench(k[b].data_ptr(), v[b].data_ptr(), H * D * esz, k.stride(2) * esz,
+                                          idx[b].data_ptr(), T, K, T, sink[b * T:].data_ptr(),
+                                          stream.cuda_stream)
+            _lib.check(rc)
+
+    for _ in range(3):
+        run()
+    ms = time_events(run, steps, flush, stream)
+    return 2.0 * B * T * K * H * D * esz / (ms / 1e3) / 1e9
+
+
+def config_measurement(name: str, dev, flush: torch.Tensor, steps: int) -> dict:
+    """One more configuration on this GPU (fused step and its two kernels), for configs beyond cfg2."""
+    from wayfinder_attention_b200.causal_topk import _launch_topk
+    from wayfinder_attention_b200.fused_sparse import _launch_attention, fused_sparse_attention
+
+    w = CONFIGS[name]
+    x = device_inputs(w, dev)
+    stream = torch.cuda.current_stream(dev)
+    scale = w.D ** -0.5
+    idx = torch.empty(w.B, w.T, min(w.K, w.T), dtype=torch.int32, device=dev)
+    step = lambda: fused_sparse_attention(x["q_addr"], x["k_addr"], x["q"], x["k"], x["v"], w.K, scale)  # noqa: E731
+    for _ in range(3):
+        step()
+    ms = time_events(step, steps, flush, stream)
+    topk_ms = time_events(lambda: _launch_topk(x["q_addr"], x["k_addr"], w.K, "reference", out=idx), steps, flush,
+                          stream)
+    attn_ms = time_events(lambda: _launch_attention(x["q"], x["k"], x["v"], idx, scale, mask_negative=False,
+                                                    out_dtype=None), steps, flush, stream)
+    peaks, kind = load_peaks()
+    kv_bytes = 2.0 * w.B * w.T * w.H * w.D * x["k"].element_size()
+    res = {"ms": ms, "queries_per_s": w.queries / (ms / 1e3), "B": w.B, "H": w.H, "T": w.T, "D": w.D, "K": w.K,
+           "kernels_ms": {"causal_topk": topk_ms, "sparse_attention": attn_ms},
+           "gathered_bytes": w.gathered_bytes(), "kv_bytes": kv_bytes,
+           "gathered_gbs": w.gathered_bytes() / (attn_ms / 1e3) / 1e9}
+    dram = ATTN_DRAM_BYTES.get(name)
+    if dram is not None:
+        gbs = dram / (attn_ms / 1e3) / 1e9
+        res["hbm"] = {"dram_bytes": dram, "source": ATTN_DRAM_SOURCE[name], "achieved_gbs": gbs,
+                      "peak_gbs": float(peaks["hbm_gbs"]), "frac": gbs / float(peaks["hbm_gbs"]),
+                      "peak_kind": kind}
+    del x
+    torch.cuda.empty_cache()
+    return res
 
 
 def decoder_forward(B: int, T: int, flush: torch.Tensor, steps: int, dev, attention_type: str = "learned_address") -> dict:

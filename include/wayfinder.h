@@ -107,7 +107,7 @@ WF_API size_t wf_causal_topk_workspace_bytes(int64_t B, int64_t Tq, int64_t Tk, 
  * fits when wf_causal_topk_workspace_bytes() for its sizes is at most 16 MiB:
  * 2044 query rows (B*Tq) for K <= 128 with bf16/fp16 addresses; fp32 addresses also
  * keep bf16 copies of the address rows there ((Tq + Tk) * R * 2 bytes per batch
- * element), so fewer rows fit (e.g. 1792 at Tq = Tk, R = 32).  Larger requests
+ * element), so fewer rows fit (2012 at B = 1, Tq = Tk, R = 32).  Larger requests
  * return WF_ERR_UNSUPPORTED with the byte counts.  The first call on a device
  * looks up the array's device address, so make that first call before any stream
  * capture.  All calls share the one array: calls that overlap on the GPU (other
@@ -308,6 +308,18 @@ WF_API int wf_sparse_attention_backward(const void* q, const void* k, const void
                                         uint64_t drop_seed, void* dq, void* dk, void* dv, int32_t grad_dtype, const int64_t* dq_strides,
                                         const int64_t* dk_strides, const int64_t* dv_strides, void* workspace,
                                         size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Measurement aid, no counterpart in the reference: the gather-rate ceiling of the
+ * attention kernel's access pattern.  For each of n_query queries, reads the K and
+ * V rows (row_bytes each, 16..1024 in 16-byte steps, row_stride_bytes apart) at its
+ * K indices idx[q][0..K) with the attention kernel's 16-byte loads and computes
+ * nothing; one word per query goes to sink (n_query uint32).  Indices outside
+ * [0, n_rows) read row 0.  Bytes moved: 2 * n_query * K * row_bytes.
+ */
+WF_API int wf_gather_rows_bench(const void* k, const void* v, int64_t row_bytes, int64_t row_stride_bytes,
+                                const int32_t* idx, int64_t n_query, int32_t K, int64_t n_rows, uint32_t* sink,
+                                void* stream);
 
 /*
  * Test hook, no counterpart in the reference: makes the next tensor-core retrieval

@@ -23,7 +23,7 @@ SCRIPT = textwrap.dedent(
     dev = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", device_id=dev)
-    B, T, H, D, R, K, tile = 1, 4096, 4, 64, 32, 128, 256
+    B, T, H, D, R, K, tile = 2, 4096, 4, 64, 32, 128, 256
     g = torch.Generator(device=dev).manual_seed(45)
     qa = (torch.randn(B, T, R, generator=g, device=dev) / 32 ** 0.5).bfloat16()
     ka = (torch.randn(B, T, R, generator=g, device=dev) / 32 ** 0.5).bfloat16()

@@ -38,8 +38,10 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda_device):
     lib = _lib.load_library()
     f = _noalloc(lib)
     K = 128
-    for seed, T in ((45, 2000), (46, 1200)):  # the second call reuses the array left by the first
-        w = Workload("t", 1, 1, T, 16, 32, K, torch.bfloat16)
+    # the second call reuses the array left by the first; fp32 addresses also keep
+    # bf16 copies of the address rows in the array, so fewer rows fit (2012 at R=32)
+    for seed, T, dt in ((45, 2000, torch.bfloat16), (46, 1200, torch.bfloat16), (47, 2012, torch.float32)):
+        w = Workload("t", 1, 1, T, 16, 32, K, dt)
         x = to_device(make_inputs(w, seed=seed), cuda_device)
         got = torch.full((1, T, K), -7, dtype=torch.int32, device=cuda_device)
         status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
@@ -62,3 +64,8 @@ def test_noalloc_rejects_requests_beyond_its_array(cuda_device):
     rc = _call(f, x["q_addr"], x["k_addr"], K, out, status, cuda_device)
     assert rc == _lib.WF_ERR_UNSUPPORTED
     assert b"built-in" in lib.wf_last_error()
+    # fp32 addresses: 2013 rows no longer fit beside their bf16 copies
+    w = Workload("t", 1, 1, 2013, 16, 32, K, torch.float32)
+    x = to_device(make_inputs(w), cuda_device)
+    out = torch.empty(1, 2013, K, dtype=torch.int32, device=cuda_device)
+    assert _call(f, x["q_addr"], x["k_addr"], K, out, status, cuda_device) == _lib.WF_ERR_UNSUPPORTED

@@ -49,6 +49,7 @@ EXPORTED_SYMBOLS = (
     "wf_sparse_attention_cyclic_kv_chunked",
     "wf_causal_topk_noalloc",
     "wf_testing_withhold_pair_arrive",
+    "wf_gather_rows_bench",
 )
 
 _DTYPE_CODES = {
@@ -74,6 +75,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.wf_last_error.argtypes = []
     lib.wf_max_top_k.restype = ctypes.c_int
     lib.wf_max_top_k.argtypes = []
+    lib.wf_gather_rows_bench.restype = ctypes.c_int
+    lib.wf_gather_rows_bench.argtypes = [_vp, _vp, _i64, _i64, _vp, _i64, _i32, _i64, _vp, _vp]
     lib.wf_testing_withhold_pair_arrive.restype = ctypes.c_int
     lib.wf_testing_withhold_pair_arrive.argtypes = [_i32, ctypes.c_uint64]
     lib.wf_causal_topk.restype = ctypes.c_int

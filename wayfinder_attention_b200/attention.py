@@ -332,7 +332,7 @@ class RoutingSparseAttention(nn.Module):
         from .router import PerLayerRouter
 
         if isinstance(self.router, PerLayerRouter):
-            return self.router.get_router(self.layer_idx).forward_query_key(x)
+            return self.router.forward_query_key(x, self.layer_idx)
         if hasattr(self.router, "forward_query_key"):
             return self.router.forward_query_key(x)
         r = self.router(x)

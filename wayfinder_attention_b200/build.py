@@ -24,7 +24,7 @@ LIB_PATH = PKG_DIR / LIB_NAME
 
 SOURCES = ["wf_abi.cu", "wf_topk.cu", "wf_topk_tc.cu", "wf_attn.cu", "wf_attn_bf16.cu", "wf_attn_f16.cu",
            "wf_attn_f32.cu", "wf_addr_proj.cu",
-           "wf_attn_bwd.cu", "wf_keymask.cu"]
+           "wf_attn_bwd.cu", "wf_keymask.cu", "wf_bench.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

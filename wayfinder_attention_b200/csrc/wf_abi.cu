@@ -135,6 +135,19 @@ const char* wf_last_error(void) { return g_err.c_str(); }
 
 int wf_max_top_k(void) { return wf::topk_max_k(); }
 
+int wf_gather_rows_bench(const void* k, const void* v, int64_t row_bytes, int64_t row_stride_bytes,
+                         const int32_t* idx, int64_t n_query, int32_t K, int64_t n_rows, uint32_t* sink,
+                         void* stream) {
+  if (!k || !v || !idx || !sink) return fail(WF_ERR_INVALID_ARGUMENT, "wf_gather_rows_bench: null pointer");
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) % 16)
+    return fail(WF_ERR_INVALID_ARGUMENT, "wf_gather_rows_bench: rows must be 16-byte aligned");
+  const int rc = wf::launch_gather_rows_bench(k, v, row_bytes, row_stride_bytes, idx, n_query, K, n_rows, sink,
+                                              static_cast<cudaStream_t>(stream));
+  if (rc < 0) return fail(WF_ERR_UNSUPPORTED, "wf_gather_rows_bench: rows of 16..1024 bytes in 16-byte steps");
+  if (rc) return cuda_fail(rc, "wf_gather_rows_bench");
+  return ok();
+}
+
 int wf_testing_withhold_pair_arrive(int32_t round, uint64_t wait_limit_ns) {
   wf::topk_tc_test_withhold(round, wait_limit_ns);
   return ok();

@@ -128,4 +128,10 @@ size_t attn_bwd_workspace_bytes(int64_t B, int64_t H, int64_t Tq, int64_t Tk, in
 int launch_sparse_attention_backward(AttnBwdParams p, void* ws, size_t ws_bytes, int dtype, int grad_dtype,
                                      cudaStream_t stream);
 
+// Gather-rate ceiling (wf_bench.cu): K and V rows of row_bytes (<= 1024) at the
+// indices idx[n_query][K], 16-byte loads, nothing computed; -1 for bad sizes.
+int launch_gather_rows_bench(const void* k, const void* v, int64_t row_bytes, int64_t stride_bytes,
+                             const int32_t* idx, int64_t n_query, int K, int64_t n_rows, uint32_t* sink,
+                             cudaStream_t stream);
+
 }  // namespace wf

@@ -988,7 +988,7 @@ int launch_causal_topk_tc(const TopkParams& p, int dtype, cudaStream_t stream) {
 // kNoAllocScratchBytes for it until the process exits.  All calls share it and it
 // keeps the previous call's contents; nothing in it needs to start at zero,
 // because the retrieval kernel writes every count and candidate it later reads.
-constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB: B*Tq <= 2044 query rows (8208 bytes each) for K <= 128
+constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB: B*Tq <= 2044 query rows (8208 bytes each) for K <= 128; fp32 addresses add bf16 copies of the rows
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {

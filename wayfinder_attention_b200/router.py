@@ -73,23 +73,6 @@ class RouterMLP(nn.Module):
         k = self.forward(x, as_query=False) if self.similarity == "asymmetric" else q
         return q, k
 
-    def pairwise_scores(self, routing: torch.Tensor, key_routing: torch.Tensor | None = None) -> torch.Tensor:
-        """Dense (B, T, T) scores for the router's training loss (``router.py:88-103``)."""
-        key_routing = routing if key_routing is None else key_routing
-        if routing.dim() == 4:
-            scores = torch.einsum("bthq,bshq->bhts", routing, key_routing).mean(dim=2)
-        else:
-            scores = torch.matmul(routing, key_routing.transpose(-2, -1))
-        if self.use_affine_dot:
-            scores = scores * self.dot_scale + self.dot_bias
-        return scores
-
-    def retrieval_scores(self, x: torch.Tensor) -> torch.Tensor:
-        q, k = self.forward_query_key(x)
-        if q.dim() == 4:
-            return torch.einsum("bthq,bshq->bts", q, k) / q.shape[2]
-        return torch.matmul(q, k.transpose(-2, -1))
-
 
 class PerLayerRouter(nn.Module):
     """One ``RouterMLP`` per transformer layer (``router.py:118-156``)."""
@@ -110,12 +93,6 @@ class PerLayerRouter(nn.Module):
 
     def forward_query_key(self, x: torch.Tensor, layer_idx: int) -> tuple[torch.Tensor, torch.Tensor]:
         return self.routers[layer_idx].forward_query_key(x)
-
-    def retrieval_scores(self, x: torch.Tensor, layer_idx: int) -> torch.Tensor:
-        return self.routers[layer_idx].retrieval_scores(x)
-
-    def get_router(self, layer_idx: int) -> RouterMLP:
-        return self.routers[layer_idx]
 
 
 class MultiScaleRouter(nn.Module):
@@ -140,9 +117,6 @@ class MultiScaleRouter(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return torch.cat([self.local_router(x), self.global_router(x)], dim=-1)
-
-    def routing_for_loss(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        return self.local_router(x), self.global_router(x)
 
     def retrieve_indices(self, x: torch.Tensor, k: int, layer_idx: int = 0) -> torch.Tensor:
         """(B, T, k) int64 merged candidates (``router.py:185-204``), vectorised."""

@@ -98,6 +98,50 @@ def gather_sequence(x_local: torch.Tensor, tile: int, group=None) -> torch.Tenso
     return g.reshape((B, world * Tl) + rest)
 
 
+def chunked_kv_attention(q_l: torch.Tensor, idx: torch.Tensor, k_g: torch.Tensor, v_g: torch.Tensor, scale: float,
+                         tile: int, pad_mode: str = "reference", out_dtype: torch.dtype | None = None,
+                         wait=None) -> torch.Tensor:
+    """Attention of a rank's query rows over all-gathered K/V stored chunk-major.
+
+    q_l: (B, H, Tl, D) this rank's rows (``local_rows`` order); idx: (B, Tl, K) global
+    key indices; k_g, v_g: (C, W, B, Tc, H, D) with block (c, w) = rank w's local rows
+    [c*Tc, (c+1)*Tc).  Chunk c of the query rows reads key chunks <= c only (causal),
+    so chunks run in the order 1..C-1, 0 (chunk 0 last: the reference pads of rows
+    t < K-1 point ahead) and ``wait(c)``, if given, is called before chunk c is
+    enqueued — the caller makes the stream wait for that chunk's K/V there.
+    """
+    from . import _lib
+
+    C, W, B, Tc, H, D = k_g.shape
+    Tl = q_l.shape[2]
+    if Tl != C * Tc or tuple(v_g.shape) != tuple(k_g.shape) or q_l.shape[0] != B or q_l.shape[1] != H:
+        raise ValueError(f"q {tuple(q_l.shape)} does not match chunk-major K/V {tuple(k_g.shape)}")
+    T = W * Tl
+    dev = q_l.device
+    out = torch.empty(B, H, Tl, D, dtype=out_dtype or q_l.dtype, device=dev)
+    kb = k_g[0, 0].permute(0, 2, 1, 3)  # block (chunk 0, rank 0) as (B, H, Tc, D)
+    vb = v_g[0, 0].permute(0, 2, 1, 3)
+    K = idx.shape[-1]
+    lib = _lib.load_library()
+    flags = _lib.WF_ATTN_MASK_NEGATIVE if pad_mode == "masked" else 0
+    st = _lib.status_arg(dev, None)
+    with torch.cuda.device(dev):
+        for c in list(range(1, C)) + [0]:
+            if wait is not None:
+                wait(c)
+            rows = slice(c * Tc, (c + 1) * Tc)
+            qc, ic, oc = q_l[:, :, rows], idx[:, rows], out[:, :, rows]
+            rc = lib.wf_sparse_attention_cyclic_kv_chunked(
+                qc.data_ptr(), kb.data_ptr(), vb.data_ptr(), _lib.dtype_code(q_l.dtype), ic.data_ptr(),
+                B, H, Tc, T, D, K, _lib.strides(qc), _lib.strides(kb), _lib.strides(vb), _lib.strides(ic),
+                float(scale), flags, oc.data_ptr(), _lib.dtype_code(out.dtype), _lib.strides(oc),
+                tile, W, Tc, k_g.stride(1), v_g.stride(1), st, _lib.stream_ptr(dev),
+            )
+            _lib.check(rc)
+    _lib.status_after(dev, None)
+    return out
+
+
 class SequenceShardedAttention:
     """Fused retrieval + sparse attention for ONE long sequence split over ranks.
 
@@ -145,12 +189,9 @@ class SequenceShardedAttention:
         """q_addr_l, k_addr_l: (B, Tl, R); q_l, k_l, v_l: (B, H, Tl, D) views of (B, Tl, H, D) memory."""
         import torch.distributed as dist
 
-        from . import _lib
-
         world = dist.get_world_size(self.group)
         rank = dist.get_rank(self.group)
         B, H, Tl, D = q_l.shape
-        T = world * Tl
         if self.top_k > self.tile:
             raise ValueError(f"top_k={self.top_k} must not exceed the row tile {self.tile}")
         C = self._n_chunks(Tl, world)
@@ -179,27 +220,8 @@ class SequenceShardedAttention:
                 ev.record(side)
                 landed.append(ev)
         idx = sharded_causal_topk(q_addr_l, k_addr, self.top_k, world, rank, self.tile, self.pad_mode)
-        dev = q_l.device
-        out = torch.empty(B, H, Tl, D, dtype=out_dtype or q_l.dtype, device=dev)
-        kb = k_g[0, 0].permute(0, 2, 1, 3)  # block (chunk 0, rank 0) as (B, H, Tc, D)
-        vb = v_g[0, 0].permute(0, 2, 1, 3)
-        K = idx.shape[-1]
-        lib = _lib.load_library()
-        flags = _lib.WF_ATTN_MASK_NEGATIVE if self.pad_mode == "masked" else 0
-        st = _lib.status_arg(dev, None)
-        with torch.cuda.device(dev):
-            for c in list(range(1, C)) + [0]:
-                main.wait_event(landed[c] if c else landed[-1])
-                rows = slice(c * Tc, (c + 1) * Tc)
-                qc, ic, oc = q_l[:, :, rows], idx[:, rows], out[:, :, rows]
-                rc = lib.wf_sparse_attention_cyclic_kv_chunked(
-                    qc.data_ptr(), kb.data_ptr(), vb.data_ptr(), _lib.dtype_code(q_l.dtype), ic.data_ptr(),
-                    B, H, Tc, T, D, K, _lib.strides(qc), _lib.strides(kb), _lib.strides(vb), _lib.strides(ic),
-                    float(self.scale), flags, oc.data_ptr(), _lib.dtype_code(out.dtype), _lib.strides(oc),
-                    self.tile, world, Tc, k_g.stride(1), v_g.stride(1), st, _lib.stream_ptr(dev),
-                )
-                _lib.check(rc)
-        _lib.status_after(dev, None)
+        out = chunked_kv_attention(q_l, idx, k_g, v_g, self.scale, self.tile, self.pad_mode, out_dtype,
+                                   wait=lambda c: main.wait_event(landed[c] if c else landed[-1]))
         return out, idx
 
     __call__ = forward
