@@ -217,6 +217,10 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-dense", action="store_true")
     ap.add_argument("--no-decoder", action="store_true", help="skip the whole-decoder prefill measurements")
+    ap.add_argument("--profile-op", choices=["topk", "attention", "both", "fused", "backward", "projection"],
+                    help="profiling mode: run only this op --iters times on --config (L2 flushed before each) "
+                         "and print 'ok'; for ncu captures")
+    ap.add_argument("--iters", type=int, default=3, help="calls in --profile-op mode")
     ap.add_argument("--no-extra-configs", action="store_true",
                     help="skip the cfg4 / cfg5 measurements (and the sequence-sharded cfg4 run at N > 1)")
     args = ap.parse_args()
@@ -224,6 +228,9 @@ def main() -> None:
     claim_stdout()
 
     w = CONFIGS[args.config]
+    if args.profile_op:
+        profile_op(args.profile_op, w, args.iters)
+        return
     if args.impl == "reference":
         run_reference_arm(args, w)
         return
@@ -569,6 +576,46 @@ def run_sequence_sharded(args, w: Workload, rank: int, world: int, dev) -> None:
             "gpu_launches": (2 + m["chunks"]) * args.steps,  # per step: retrieval, finalisation, attention chunks
             "clocks": m["clocks"],
         })
+
+
+def profile_op(op: str, w: Workload, iters: int) -> None:
+    """One hot-path op ``iters`` times on seeded device inputs of ``w``, L2 flushed before each call.
+
+    ``projection`` runs the fused address projection at the decoder's shape (32768 x 256
+    bf16 hidden states, d_A = 32, both addresses).  Prints only a final ``ok``.
+    """
+    from wayfinder_attention_b200.causal_topk import causal_topk
+    from wayfinder_attention_b200.fused_sparse import (_launch_attention_backward, fused_sparse_attention,
+                                                       sparse_meat_attention)
+
+    dev = torch.device("cuda:0")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    if op == "projection":
+        from wayfinder_attention_b200.address_projection import address_projection
+
+        g = torch.Generator(device=dev).manual_seed(45)
+        hid = torch.randn(32768, 256, generator=g, device=dev).to(torch.bfloat16)
+        wgt = (torch.randn(64, 256, generator=g, device=dev) / 16).to(torch.bfloat16)
+        bias = torch.zeros(64, dtype=torch.bfloat16, device=dev)
+        for _ in range(iters):
+            flush.zero_()
+            address_projection(hid, wgt, bias, 32)
+    else:
+        x = device_inputs(w, dev)
+        scale = w.D ** -0.5
+        idx = causal_topk(x["q_addr"], x["k_addr"], w.K)
+        for _ in range(iters):
+            flush.zero_()
+            if op in ("topk", "both"):
+                idx = causal_topk(x["q_addr"], x["k_addr"], w.K)
+            if op in ("attention", "both"):
+                sparse_meat_attention(x["q"], x["k"], x["v"], idx, scale)
+            if op == "fused":
+                fused_sparse_attention(x["q_addr"], x["k_addr"], x["q"], x["k"], x["v"], w.K, scale)
+            if op == "backward":
+                _launch_attention_backward(x["q"], x["k"], x["v"], idx, x["q"], scale, False)
+    torch.cuda.synchronize()
+    print("ok")
 
 
 def device_inputs(w: Workload, dev, seed: int = 45) -> dict:

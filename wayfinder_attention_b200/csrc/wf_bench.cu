@@ -19,6 +19,8 @@ namespace {
 constexpr int kWarps = 8;
 constexpr int kInFlight = 4;  // retrieved rows per lane in flight, as the attention kernel keeps
 
+// FULL: rows of exactly 64 vectors (1 KB), two per lane, no per-load predicate.
+template <bool FULL>
 __global__ void __launch_bounds__(kWarps * 32) gather_rows_kernel(const uint4* __restrict__ k,
                                                                 const uint4* __restrict__ v, int64_t row_vecs,
                                                                 int64_t stride_vecs, const int32_t* __restrict__ idx,
@@ -37,13 +39,15 @@ __global__ void __launch_bounds__(kWarps * 32) gather_rows_kernel(const uint4* _
 #pragma unroll
       for (int u = 0; u < kInFlight; ++u) {
         int j = __shfl_sync(0xffffffffu, my, (j0 + u) & 31);
-        j = (j0 + u < n && j >= 0 && j < n_rows) ? j : 0;
+        if (!FULL) j = (j0 + u < n && j >= 0 && j < n_rows) ? j : 0;
+        else j = (j >= 0 && j < n_rows) ? j : 0;
         const int64_t base = (int64_t)j * stride_vecs;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int64_t e = lane + 32 * c;
-          a[u][c] = e < row_vecs ? __ldg(k + base + e) : make_uint4(0, 0, 0, 0);
-          b[u][c] = e < row_vecs ? __ldg(v + base + e) : make_uint4(0, 0, 0, 0);
+          const bool in = FULL || e < row_vecs;
+          a[u][c] = in ? __ldg(k + base + e) : make_uint4(0, 0, 0, 0);
+          b[u][c] = in ? __ldg(v + base + e) : make_uint4(0, 0, 0, 0);
         }
       }
 #pragma unroll
@@ -65,9 +69,9 @@ int launch_gather_rows_bench(const void* k, const void* v, int64_t row_bytes, in
   if (row_bytes <= 0 || row_bytes > 1024 || row_bytes % 16 || stride_bytes % 16 || K < 1 || n_query < 1)
     return -1;
   const unsigned blocks = (unsigned)((n_query + kWarps - 1) / kWarps);
-  gather_rows_kernel<<<blocks, kWarps * 32, 0, stream>>>(static_cast<const uint4*>(k), static_cast<const uint4*>(v),
-                                                          row_bytes / 16, stride_bytes / 16, idx, n_query, K, n_rows,
-                                                          sink);
+  auto kern = (row_bytes == 1024 && K % 32 == 0) ? gather_rows_kernel<true> : gather_rows_kernel<false>;
+  kern<<<blocks, kWarps * 32, 0, stream>>>(static_cast<const uint4*>(k), static_cast<const uint4*>(v), row_bytes / 16,
+                                          stride_bytes / 16, idx, n_query, K, n_rows, sink);
   return (int)cudaGetLastError();
 }
 
