@@ -330,6 +330,7 @@ def main() -> None:
     h2d = sum(v.numel() * v.element_size() for v in pin.values())
     d2h = out_h.numel() * out_h.element_size() + idx_h.numel() * idx_h.element_size()
     host_op = HostFusedSparseAttention(K, scale, chunks=E2E_CHUNKS, device=dev)
+    host_op_out = HostFusedSparseAttention(K, scale, chunks=E2E_CHUNKS, device=dev, download_indices=False)
 
     def e2e_serial():
         for k_ in pin:
@@ -342,6 +343,9 @@ def main() -> None:
     def e2e_pipelined():
         host_op(pin["q_addr"], pin["k_addr"], *(pin[n].transpose(1, 2) for n in ("q", "k", "v")),
                 out=out_h, idx_out=idx_h)
+
+    def e2e_pipelined_out_only():
+        host_op_out(pin["q_addr"], pin["k_addr"], *(pin[n].transpose(1, 2) for n in ("q", "k", "v")), out=out_h)
 
     def time_e2e(fn):
         for _ in range(args.warmup):
@@ -382,6 +386,7 @@ def main() -> None:
 
     e2e_serial_ms = time_e2e(e2e_serial)
     e2e_ms_step = time_e2e(e2e_pipelined)
+    e2e_out_only_ms = time_e2e(e2e_pipelined_out_only)
     copy_ms = time_e2e(copies_only)
     e2e_value = queries / (e2e_ms_step / 1e3)
 
@@ -448,6 +453,8 @@ def main() -> None:
                     "ms_per_step": e2e_ms_step, "api": "HostFusedSparseAttention (copies overlapped, "
                     f"{E2E_CHUNKS} row chunks)", "serial_ms_per_step": e2e_serial_ms,
                     "copies_only_ms_per_step": copy_ms,
+                    "out_only_ms_per_step": e2e_out_only_ms,
+                    "out_only_d2h_bytes_per_step": out_h.numel() * out_h.element_size(),
                     "host_link_gbs_per_rank": (h2d + d2h) / (copy_ms / 1e3) / 1e9,
                     "frac_of_copy_ceiling": copy_ms / e2e_ms_step,
                     "note": "copies_only: the same uploads and downloads on every rank at once, no kernels"},

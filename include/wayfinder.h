@@ -227,7 +227,8 @@ WF_API int wf_fused_sparse_attention(const void* q_addr, const void* k_addr, int
  *   q_h, k_h, v_h      : (B, H, T, D) host tensors with element strides q/k/v_strides,
  *                        stride(D) = 1 and either (B,T,H,D)-major rows (stride(T) = H*D,
  *                        stride(H) = D) or head-major rows (stride(T) = D)
- *   idx_h              : (B, T, K_eff) int32 host output, contiguous
+ *   idx_h              : (B, T, K_eff) int32 host output, contiguous; NULL leaves the
+ *                        indices in d_idx only (no download)
  *   out_h              : (B, H, T, D) host output with out_strides (same layout rule)
  *   d_*                : device staging buffers of the same shapes and strides as the host
  *                        tensors (addresses and idx contiguous), reused across calls

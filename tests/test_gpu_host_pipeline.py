@@ -99,6 +99,21 @@ def test_host_pipeline_against_oracle_and_outputs_given():
     np.testing.assert_allclose(out.numpy(), o_ref, rtol=1e-5, atol=1e-5)
 
 
+def test_host_pipeline_without_index_download():
+    from wayfinder_attention_b200 import HostFusedSparseAttention, fused_sparse_attention
+
+    B, H, T, D, R, K = 1, 4, 1500, 64, 32, 64
+    qa, ka, qkv = _inputs(B, H, T, D, R, torch.bfloat16, 21)
+    q, k, v = (x.pin_memory().transpose(1, 2) for x in qkv)
+    op = HostFusedSparseAttention(K, D ** -0.5, chunks=4, device=0, download_indices=False)
+    out_h, idx_h = op(qa.pin_memory(), ka.pin_memory(), q, k, v)
+    torch.cuda.current_stream().synchronize()
+    assert idx_h is None and op.last_indices.is_cuda
+    ref_out, ref_idx = fused_sparse_attention(qa.cuda(), ka.cuda(), q.cuda(), k.cuda(), v.cuda(), K, D ** -0.5)
+    assert torch.equal(op.last_indices, ref_idx)
+    assert torch.equal(out_h, ref_out.cpu())
+
+
 def test_host_pipeline_rejects_device_inputs():
     from wayfinder_attention_b200 import HostFusedSparseAttention
 

@@ -402,7 +402,7 @@ int wf_fused_sparse_attention_host(const void* q_addr_h, const void* k_addr_h, i
                                    size_t workspace_bytes, int32_t* status, void* stream, void* h2d_stream,
                                    void* d2h_stream) {
   if (top_k < 1) return fail(WF_ERR_INVALID_ARGUMENT, "wf_fused_sparse_attention_host: top_k must be >= 1, got %d", top_k);
-  if (!q_addr_h || !k_addr_h || !q_h || !k_h || !v_h || !idx_h || !out_h || !d_q_addr || !d_k_addr || !d_q ||
+  if (!q_addr_h || !k_addr_h || !q_h || !k_h || !v_h || !out_h || !d_q_addr || !d_k_addr || !d_q ||
       !d_k || !d_v || !d_idx || !d_out || !q_strides || !k_strides || !v_strides || !out_strides)
     return fail(WF_ERR_INVALID_ARGUMENT, "wf_fused_sparse_attention_host: null pointer argument");
   if (B < 1 || H < 1 || T < 1) return fail(WF_ERR_INVALID_ARGUMENT, "wf_fused_sparse_attention_host: empty problem");
@@ -467,7 +467,8 @@ int wf_fused_sparse_attention_host(const void* q_addr_h, const void* k_addr_h, i
   WF_EV(e_idx);
   WF_CK(cudaEventRecord(e_idx, sm));
   WF_CK(cudaStreamWaitEvent(so, e_idx, 0));
-  WF_CK(cudaMemcpyAsync(idx_h, d_idx, (size_t)(B * T) * k_eff * sizeof(int32_t), cudaMemcpyDeviceToHost, so));
+  if (idx_h)  // NULL: the indices stay in d_idx only
+    WF_CK(cudaMemcpyAsync(idx_h, d_idx, (size_t)(B * T) * k_eff * sizeof(int32_t), cudaMemcpyDeviceToHost, so));
   // Chunk c's causal indices read K/V rows < e only, so it needs uploads 0..c.  With
   // pad_mode=reference, rows i < K-1 also attend their pad rows (i + K + s + 1) % T,
   // s < K, which reach row 3K-2 (and wrap to any row when 3K-2 >= T): a chunk holding

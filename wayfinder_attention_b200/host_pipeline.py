@@ -39,25 +39,29 @@ class HostFusedSparseAttention:
 
     ``chunks`` is the number of query-row chunks the sequence is split into for
     the pipeline.  Device staging buffers and streams persist between calls of
-    the same shapes.  ``__call__`` enqueues everything behind the current stream
+    the same shapes.  With ``download_indices=False`` the retrieved indices stay on
+    the device (``last_indices``) and the call returns ``(out, None)``: a third less
+    to download at K=128, H*D=512.  ``__call__`` enqueues everything behind the current stream
     and makes the current stream wait for the downloads, so the host outputs are
     valid after ``torch.cuda.current_stream().synchronize()``.
     """
 
     def __init__(self, top_k: int, scale: float, *, chunks: int = 8, pad_mode: str = "reference",
-                 device: torch.device | str | int = 0):
+                 device: torch.device | str | int = 0, download_indices: bool = True):
         if chunks < 1:
             raise ValueError(f"chunks must be >= 1, got {chunks}")
         self.top_k = int(top_k)
         self.scale = float(scale)
         self.chunks = int(chunks)
         self.pad_mode = pad_mode
+        self.download_indices = bool(download_indices)
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         self._bufs: dict[str, torch.Tensor] = {}
         self._key = None
         self._s_in = self._s_out = None
         self._ws = None
         self._ws_key = None
+        self.last_indices: torch.Tensor | None = None
 
     def _staging(self, tensors: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
         key = tuple((n, tuple(t.shape), tuple(t.stride()), t.dtype) for n, t in tensors.items())
@@ -86,19 +90,21 @@ class HostFusedSparseAttention:
         k_eff = min(self.top_k, T)
         if out is None:
             out = torch.empty(B, T, H, D, dtype=q.dtype, pin_memory=True).transpose(1, 2)
-        if idx_out is None:
+        if idx_out is None and self.download_indices:
             idx_out = torch.empty(B, T, max(k_eff, 0), dtype=torch.int32, pin_memory=True)
-        if tuple(out.shape) != (B, H, T, D) or tuple(idx_out.shape) != (B, T, max(k_eff, 0)):
-            raise ValueError("out / idx_out have the wrong shape")
-        if not idx_out.is_contiguous() or idx_out.dtype != torch.int32:
-            raise ValueError("idx_out must be a contiguous int32 tensor")
+        if tuple(out.shape) != (B, H, T, D):
+            raise ValueError("out has the wrong shape")
+        if idx_out is not None and (tuple(idx_out.shape) != (B, T, max(k_eff, 0)) or not idx_out.is_contiguous()
+                                    or idx_out.dtype != torch.int32):
+            raise ValueError(f"idx_out must be a contiguous int32 tensor of shape {(B, T, max(k_eff, 0))}")
         if k_eff <= 0 or B == 0 or H == 0:
             out.zero_()  # softmax over an empty set: the reference's sum over zero rows
             return out, idx_out
         dev = self.device
         qa_h, ka_h, _ = promote_compute_dtype(q_search, k_search, None)
         qa_h, ka_h = qa_h.contiguous(), ka_h.contiguous()
-        d = self._staging({"qa": qa_h, "ka": ka_h, "q": q, "k": k, "v": v, "out": out, "idx": idx_out})
+        idx_like = idx_out if idx_out is not None else torch.empty(B, T, k_eff, dtype=torch.int32)
+        d = self._staging({"qa": qa_h, "ka": ka_h, "q": q, "k": k, "v": v, "out": out, "idx": idx_like})
         if self._ws is None or self._ws_key != (B, T, R, self.top_k, qa_h.dtype):
             self._ws = _lib.workspace(B, T, T, R, self.top_k, qa_h.dtype, dev)
             self._ws_key = (B, T, R, self.top_k, qa_h.dtype)
@@ -113,7 +119,8 @@ class HostFusedSparseAttention:
                 qa_h.data_ptr(), ka_h.data_ptr(), _lib.dtype_code(qa_h.dtype), R,
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.dtype_code(q.dtype), B, H, T, D,
                 _lib.strides(q), _lib.strides(k), _lib.strides(v), self.top_k, self.scale,
-                pad_mode_code(self.pad_mode), min(self.chunks, T, 64), idx_out.data_ptr(), out.data_ptr(),
+                pad_mode_code(self.pad_mode), min(self.chunks, T, 64),
+                idx_out.data_ptr() if idx_out is not None else None, out.data_ptr(),
                 _lib.dtype_code(out.dtype), _lib.strides(out),
                 d["qa"].data_ptr(), d["ka"].data_ptr(), d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(),
                 d["idx"].data_ptr(), d["out"].data_ptr(), ws.data_ptr() if ws is not None else None,
@@ -122,6 +129,7 @@ class HostFusedSparseAttention:
             )
         _lib.check(rc)
         _lib.status_after(dev, None)
+        self.last_indices = d["idx"]
         return out, idx_out
 
     forward = __call__
