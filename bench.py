@@ -475,6 +475,8 @@ def main() -> None:
         if seq is not None:
             result["cfg4_sequence_sharded"] = seq
         if world == 1 and not args.no_extra_configs:
+            result["overlap_probe"] = overlap_probe(w, dev, flush, args.steps)
+        if world == 1 and not args.no_extra_configs:
             # configurations whose K/V outgrow the 126 MB L2 (cfg4: 1.07 GB; cfg5: 2.1 GB per call)
             result["cfg4_single_gpu"] = config_measurement("cfg4", dev, flush, max(3, args.steps // 4))
             result["cfg5_k128"] = config_measurement("cfg5", dev, flush, max(3, args.steps // 4))
@@ -623,6 +625,49 @@ def profile_op(op: str, w: Workload, iters: int) -> None:
                 _launch_attention_backward(x["q"], x["k"], x["v"], idx, x["q"], scale, False)
     torch.cuda.synchronize()
     print("ok")
+
+
+def overlap_probe(w: Workload, dev, flush: torch.Tensor, steps: int) -> dict:
+    """Retrieval and attention of two independent cfg2 problems, serial and on two streams at once.
+
+    If the two kernels left each other's resources idle, the concurrent form would
+    approach max(topk, attention); it stays near their sum, which is why this build
+    does not fuse retrieval with attention per query tile.
+    """
+    from wayfinder_attention_b200.causal_topk import _launch_topk
+    from wayfinder_attention_b200.fused_sparse import _launch_attention
+
+    x1, x2 = device_inputs(w, dev, 1), device_inputs(w, dev, 2)
+    i1 = torch.empty(w.B, w.T, w.K, dtype=torch.int32, device=dev)
+    i2 = torch.empty_like(i1)
+    _launch_topk(x2["q_addr"], x2["k_addr"], w.K, "reference", out=i2)
+    main = torch.cuda.current_stream(dev)
+    s1, s2 = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    topk = lambda: _launch_topk(x1["q_addr"], x1["k_addr"], w.K, "reference", out=i1)  # noqa: E731
+    attn = lambda: _launch_attention(x2["q"], x2["k"], x2["v"], i2, w.D ** -0.5, mask_negative=False,  # noqa: E731
+                                     out_dtype=None)
+
+    def both_serial():
+        topk()
+        attn()
+
+    def both_concurrent():
+        s1.wait_stream(main)
+        s2.wait_stream(main)
+        with torch.cuda.stream(s1):
+            topk()
+        with torch.cuda.stream(s2):
+            attn()
+        main.wait_stream(s1)
+        main.wait_stream(s2)
+
+    res = {}
+    for name, fn in (("topk_ms", topk), ("attention_ms", attn), ("serial_ms", both_serial),
+                     ("concurrent_ms", both_concurrent)):
+        for _ in range(3):
+            fn()
+        res[name] = time_events(fn, steps, flush, main)
+    return res
 
 
 def device_inputs(w: Workload, dev, seed: int = 45) -> dict:

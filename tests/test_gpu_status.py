@@ -59,15 +59,35 @@ def test_timeout_raises_without_a_status_word(cuda_device):
     assert torch.equal(idx, ref_idx) and torch.equal(out, ref_out)
 
 
-def test_out_of_range_index_raises_at_the_next_call(cuda_device):
+def test_out_of_range_index_raises_at_check(cuda_device):
     from wayfinder_attention_b200 import check_status, sparse_meat_attention
 
     g = torch.Generator().manual_seed(2)
     q, k, v = (torch.randn(1, 2, 64, 32, generator=g).cuda() for _ in range(3))
     idx = torch.zeros(1, 64, 4, dtype=torch.int32)
     idx[0, 5, 1] = 64  # one past the last key
-    sparse_meat_attention(q, k, v, idx.cuda(), 0.2)
-    torch.cuda.synchronize()
+    check_status()
+    out = sparse_meat_attention(q, k, v, idx.cuda(), 0.2)
     with pytest.raises(RuntimeError, match="out of range"):
-        sparse_meat_attention(q, k, v, torch.zeros(1, 64, 4, dtype=torch.int32, device="cuda"), 0.2)
+        check_status()
+    assert torch.isnan(out[0, :, 5]).all() and not torch.isnan(out[0, :, 4]).any()
+    check_status()
+
+
+def test_fault_surfaces_at_a_later_call_without_check(cuda_device):
+    """Without check_status the fault still reaches the caller: the first launch after
+    a read-back interval queues the status copy, and the call after it raises."""
+    from wayfinder_attention_b200 import _lib, check_status, sparse_meat_attention
+
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(1, 2, 64, 32, generator=g).cuda() for _ in range(3))
+    good = torch.zeros(1, 64, 4, dtype=torch.int32, device="cuda")
+    bad = good.clone()
+    bad[0, 7, 0] = -1000  # below -Tk: out of range
+    check_status()
+    sparse_meat_attention(q, k, v, bad, 0.2)
+    with pytest.raises(RuntimeError, match="out of range"):
+        for _ in range(2 * _lib.READBACK_CALLS + 2):
+            sparse_meat_attention(q, k, v, good, 0.2)
+            torch.cuda.synchronize()
     check_status()

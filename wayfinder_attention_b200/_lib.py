@@ -10,6 +10,7 @@ from __future__ import annotations
 import ctypes
 import os
 import threading
+import time
 from pathlib import Path
 
 import torch
@@ -208,13 +209,17 @@ def require_cuda(*tensors: torch.Tensor) -> torch.device:
 # Every kernel reports faults it can detect without stopping (an out-of-range
 # attention index: bit 0; a bounded wait that gave up: bit 1, plus a bit naming the
 # wait site from bit 4 up) by OR-ing bits into a caller-provided int32 status word.
-# A caller that passes none gets this per-device word: after each launch its value
-# is copied asynchronously into pinned host memory, and the next call on the device
-# (or ``check_status``) raises ``RuntimeError`` once that copy has landed.  No call
-# synchronises the host; ``check_status`` does, explicitly.
+# A caller that passes none gets this per-device word.  Its value is copied
+# asynchronously into pinned host memory after a launch — after the first launch,
+# then at most every READBACK_CALLS launches or READBACK_SECONDS, so the copy costs
+# nothing measurable — and a later call on the device raises ``RuntimeError`` once
+# that copy has landed.  ``check_status`` copies, waits and raises at once.  No
+# call synchronises the host except ``check_status``.
 
 STATUS_INDEX_OUT_OF_RANGE = 1
 STATUS_WAIT_TIMEOUT = 2
+READBACK_CALLS = 64
+READBACK_SECONDS = 0.05
 
 
 class _DeviceStatus:
@@ -224,8 +229,12 @@ class _DeviceStatus:
         self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self.event = torch.cuda.Event()
         self.pending = False
+        self.calls = 0
+        self.last = float("-inf")
 
     def poll(self, wait: bool = False) -> None:
+        if wait:
+            self.readback()
         if not self.pending:
             return
         if wait:
@@ -239,11 +248,20 @@ class _DeviceStatus:
                 self.word.zero_()
             raise RuntimeError(describe_status(bits))
 
-    def after_launch(self) -> None:
+    def readback(self) -> None:
         with torch.cuda.device(self.dev):
             self.host.copy_(self.word, non_blocking=True)
             self.event.record()
         self.pending = True
+        self.calls = 0
+        self.last = time.monotonic()
+
+    def after_launch(self) -> None:
+        self.calls += 1
+        if self.pending:
+            return  # the last read-back has not been looked at yet
+        if self.calls >= READBACK_CALLS or time.monotonic() - self.last >= READBACK_SECONDS:
+            self.readback()
 
 
 _status: dict[int, _DeviceStatus] = {}
