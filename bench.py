@@ -495,16 +495,19 @@ def main() -> None:
         emit(result)
 
 
-def sequence_sharded_measure(w: Workload, rank: int, world: int, dev, steps: int, warmup: int) -> dict:
-    """cfg4 on ``world`` ranks: query-row blocks cyclic over ranks, k_addr and K/V all-gathered.
+def sequence_sharded_measure(w: Workload, rank: int, world: int, dev, steps: int, warmup: int,
+                             transports=("peer", "nccl")) -> dict:
+    """cfg4 on ``world`` ranks: query-row blocks cyclic over ranks, k_addr and K/V exchanged.
 
-    Returns the per-step time (max over ranks, CUDA events, L2 flushed before each
-    step) and, for the limiter, the parts timed alone: the K/V all-gathers, the
-    rank's retrieval and its attention over landed K/V.
+    For each K/V transport (copy-engine pulls from the peers' buffers, or NCCL
+    all-gathers) returns the per-step time (max over ranks, CUDA events, L2 flushed
+    before each step) and, for the limiter, the parts timed alone: the K/V
+    exchange, the rank's retrieval (with its address all-gather) and its attention
+    over landed K/V.  The first transport is the headline.
     """
     import torch.distributed as dist
 
-    from wayfinder_attention_b200.sharding import (SequenceShardedAttention, _all_gather_rows, chunked_kv_attention,
+    from wayfinder_attention_b200.sharding import (SequenceShardedAttention, _all_gather_rows, _chunked_attention,
                                                    gather_sequence, local_rows, sharded_causal_topk)
 
     tile = 256
@@ -516,16 +519,13 @@ def sequence_sharded_measure(w: Workload, rank: int, world: int, dev, steps: int
     q_l, k_l, v_l = (full[n].transpose(1, 2)[:, rows].contiguous().transpose(1, 2) for n in ("q", "k", "v"))
     del full
     torch.cuda.empty_cache()
-    op = SequenceShardedAttention(w.K, w.D ** -0.5, tile=tile)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
-    for _ in range(warmup):
-        flush.zero_()
-        op(qa_l, ka_l, q_l, k_l, v_l)
-    torch.cuda.synchronize()
 
     def timed(fn):
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for _ in range(2):  # warm-up (first collectives of a kind set up their channels)
+            fn()
         torch.cuda.synchronize()
         dist.barrier()
         for a, b in ev:
@@ -539,29 +539,58 @@ def sequence_sharded_measure(w: Workload, rank: int, world: int, dev, steps: int
         dist.all_reduce(tot, op=dist.ReduceOp.MAX)
         return tot.item() / steps
 
-    with ClockSampler(int(os.environ.get("LOCAL_RANK", 0))) as clk:
-        ms = timed(lambda: op(qa_l, ka_l, q_l, k_l, v_l))
-    # the parts alone (same buffers and chunking as the op)
-    k_g, v_g = op._kg, op._vg
-    C, Tc = k_g.shape[0], k_g.shape[3]
     kt, vt = k_l.transpose(1, 2), v_l.transpose(1, 2)
-
-    def gathers():
-        for c in range(C):
-            _all_gather_rows(kt[:, c * Tc:(c + 1) * Tc], world, None, k_g[c])
-            _all_gather_rows(vt[:, c * Tc:(c + 1) * Tc], world, None, v_g[c])
-
     k_addr = gather_sequence(ka_l, tile)
     idx = sharded_causal_topk(qa_l, k_addr, w.K, world, rank, tile)
-    gather_ms = timed(gathers)
     retrieval_ms = timed(lambda: sharded_causal_topk(qa_l, gather_sequence(ka_l, tile), w.K, world, rank, tile))
-    attention_ms = timed(lambda: chunked_kv_attention(q_l, idx, k_g, v_g, w.D ** -0.5, tile))
     kv_recv = 2.0 * (world - 1) / world * w.B * w.T * w.H * w.D * q_l.element_size()
-    return {"ms": ms, "n_gpus": world, "chunks": C, "clocks": clk.summary(),
-            "parts_ms": {"kv_allgather": gather_ms, "retrieval_with_addr_gather": retrieval_ms,
-                         "attention": attention_ms},
-            "kv_bytes_received_per_rank": kv_recv,
-            "kv_allgather_gbs_per_rank": kv_recv / (gather_ms / 1e3) / 1e9}
+    res = {"n_gpus": world, "kv_bytes_received_per_rank": kv_recv}
+    for i, transport in enumerate(transports):
+        op = SequenceShardedAttention(w.K, w.D ** -0.5, tile=tile, transport=transport)
+        for _ in range(warmup):
+            flush.zero_()
+            op(qa_l, ka_l, q_l, k_l, v_l)
+        torch.cuda.synchronize()
+        with ClockSampler(int(os.environ.get("LOCAL_RANK", 0))) as clk:
+            ms = timed(lambda: op(qa_l, ka_l, q_l, k_l, v_l))
+        # the parts alone, same buffers and chunking as the op
+        C = op._n_chunks(q_l.shape[2], world)
+        Tc = q_l.shape[2] // C
+        shape = (C, world, w.B, Tc, w.H, w.D)
+        if transport == "peer":
+            peer = op._peer
+            side = torch.cuda.Stream(device=dev)
+
+            def exchange():
+                side.wait_stream(stream)
+                peer.exchange(kt, vt, side)
+                for e in peer.events:
+                    stream.wait_event(e)
+
+            kb, vb = peer.k_base, peer.v_base
+        else:
+            k_g, v_g = op._kg, op._vg
+
+            def exchange():
+                for c in range(C):
+                    _all_gather_rows(kt[:, c * Tc:(c + 1) * Tc], world, None, k_g[c])
+                    _all_gather_rows(vt[:, c * Tc:(c + 1) * Tc], world, None, v_g[c])
+
+            kb, vb = k_g.data_ptr(), v_g.data_ptr()
+        exchange_ms = timed(exchange)
+        attention_ms = timed(lambda: _chunked_attention(q_l, idx, kb, vb, shape, w.D ** -0.5, tile, "reference",
+                                                        None, None))
+        op.close()
+        r = {"ms": ms, "chunks": C, "clocks": clk.summary(),
+             "parts_ms": {"kv_exchange": exchange_ms, "retrieval_with_addr_gather": retrieval_ms,
+                          "attention": attention_ms},
+             "kv_exchange_gbs_per_rank": kv_recv / (exchange_ms / 1e3) / 1e9}
+        if i == 0:
+            res.update(r)
+            res["transport"] = transport
+        else:
+            res[transport] = r
+    return res
 
 
 def run_sequence_sharded(args, w: Workload, rank: int, world: int, dev) -> None:
@@ -581,7 +610,7 @@ def run_sequence_sharded(args, w: Workload, rank: int, world: int, dev) -> None:
                                       "k_addr and K/V all-gathered with NCCL",
                        "l2": "flushed before every timed step"},
             "path_roofline": {"roofline_ms_per_gpu": roof_ms, "frac": roof_ms / ms, "peak_kind": peak_kind},
-            "parts_ms": m["parts_ms"],
+            "parts_ms": m["parts_ms"], "transport": m["transport"], "nccl_transport": m.get("nccl"),
             "gpu_launches": (2 + m["chunks"]) * args.steps,  # per step: retrieval, finalisation, attention chunks
             "clocks": m["clocks"],
         })

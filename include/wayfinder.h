@@ -311,6 +311,37 @@ WF_API int wf_sparse_attention_backward(const void* q, const void* k, const void
                                         size_t workspace_bytes, int32_t* status, void* stream);
 
 /*
+ * Peer-memory K/V exchange of the sequence-sharded path, one process per GPU of a
+ * node.  No counterpart in the reference (single-GPU); it replaces the NCCL
+ * all-gather of the K/V row shards with copy-engine pulls over NVLink, which leave
+ * the SMs to retrieval and attention.
+ *   wf_peer_buffer_alloc : cudaMalloc `bytes` and export a 64-byte CUDA IPC handle
+ *   wf_peer_buffer_open  : map another process's buffer from its handle (close with
+ *                          wf_peer_buffer_close before that process frees it)
+ *   wf_pack_row_blocks   : copy this rank's (B, Tl) rows of row_bytes each (batch
+ *                          stride src_batch_stride_bytes) into blocks (c, rank) of a
+ *                          chunk-major buffer: block (c, r) of Tl/chunks rows per batch
+ *                          element at base + c*chunk_stride + r*rank_stride
+ *   wf_peer_pull_blocks  : for every chunk c, copy blocks (c, p) of every tensor t from
+ *                          each peer p's buffer (bases[p], mapped) into the same place of
+ *                          bases[rank]; chunk c's copies go to streams[c % n_streams],
+ *                          which first wait start_event (NULL: none), and chunk_events[c]
+ *                          is recorded after them.  The caller orders the pulls after every
+ *                          rank packed its blocks, and its next pack after every rank's
+ *                          pulls (e.g. with a small collective on each side).
+ */
+WF_API int wf_peer_buffer_alloc(size_t bytes, void** ptr, void* handle_out);
+WF_API int wf_peer_buffer_free(void* ptr);
+WF_API int wf_peer_buffer_open(const void* handle, void** ptr);
+WF_API int wf_peer_buffer_close(void* ptr);
+WF_API int wf_pack_row_blocks(void* base, const void* src, int64_t B, int64_t Tl, int64_t row_bytes,
+                              int64_t src_batch_stride_bytes, int32_t chunks, int64_t chunk_stride,
+                              int64_t rank_stride, int32_t rank, void* stream);
+WF_API int wf_peer_pull_blocks(void* const* bases, int32_t world, int32_t rank, int32_t chunks, int32_t tensors,
+                               int64_t block_bytes, int64_t rank_stride, int64_t chunk_stride, int64_t tensor_stride,
+                               void* start_event, void* const* streams, int32_t n_streams, void* const* chunk_events);
+
+/*
  * Measurement aid, no counterpart in the reference: the gather-rate ceiling of the
  * attention kernel's access pattern.  For each of n_query queries, reads the K and
  * V rows (row_bytes each, 16..1024 in 16-byte steps, row_stride_bytes apart) at its

@@ -30,11 +30,20 @@ SCRIPT = textwrap.dedent(
     qkv = [torch.randn(B, T, H, D, generator=g, device=dev).bfloat16() for _ in range(3)]
     full_out, full_idx = fused_sparse_attention(qa, ka, *(t.transpose(1, 2) for t in qkv), K, D ** -0.5)
     rows = torch.from_numpy(local_rows(T, world, rank, tile)).to(dev)
-    op = SequenceShardedAttention(K, D ** -0.5, tile=tile, chunks=8)  # 8 K/V chunks of 256 local rows
-    out, idx = op(qa[:, rows].contiguous(), ka[:, rows].contiguous(),
-                  *(t[:, rows].contiguous().transpose(1, 2) for t in qkv))
-    ok = torch.equal(idx, full_idx[:, rows]) and torch.equal(out, full_out[:, :, rows])
-    print(f"rank {rank} ok={ok}", flush=True)
+    ok = True
+    for transport in ("nccl", "peer"):
+        for chunks in (8, 1):  # 8 K/V chunks of 256 local rows, or one
+            op = SequenceShardedAttention(K, D ** -0.5, tile=tile, chunks=chunks, transport=transport)
+            local = [t[:, rows].contiguous().transpose(1, 2) for t in qkv]
+            # a first call on other K/V, then the real one reusing the exchange buffers:
+            # a pull or pack racing across the two calls would show in the second result
+            op(qa[:, rows].contiguous(), ka[:, rows].contiguous(), local[0], local[1] * 3, local[2] * -2)
+            out, idx = op(qa[:, rows].contiguous(), ka[:, rows].contiguous(), *local)
+            torch.cuda.synchronize()
+            good = torch.equal(idx, full_idx[:, rows]) and torch.equal(out, full_out[:, :, rows])
+            print(f"rank {rank} {transport} chunks={chunks} ok={good}", flush=True)
+            ok = ok and good
+            op.close()
     dist.barrier(); dist.destroy_process_group()
     sys.exit(0 if ok else 1)
     """

@@ -51,6 +51,12 @@ EXPORTED_SYMBOLS = (
     "wf_causal_topk_noalloc",
     "wf_testing_withhold_pair_arrive",
     "wf_gather_rows_bench",
+    "wf_peer_buffer_alloc",
+    "wf_peer_buffer_free",
+    "wf_peer_buffer_open",
+    "wf_peer_buffer_close",
+    "wf_pack_row_blocks",
+    "wf_peer_pull_blocks",
 )
 
 _DTYPE_CODES = {
@@ -76,6 +82,19 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.wf_last_error.argtypes = []
     lib.wf_max_top_k.restype = ctypes.c_int
     lib.wf_max_top_k.argtypes = []
+    lib.wf_peer_buffer_alloc.restype = ctypes.c_int
+    lib.wf_peer_buffer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(_vp), _vp]
+    lib.wf_peer_buffer_free.restype = ctypes.c_int
+    lib.wf_peer_buffer_free.argtypes = [_vp]
+    lib.wf_peer_buffer_open.restype = ctypes.c_int
+    lib.wf_peer_buffer_open.argtypes = [_vp, ctypes.POINTER(_vp)]
+    lib.wf_peer_buffer_close.restype = ctypes.c_int
+    lib.wf_peer_buffer_close.argtypes = [_vp]
+    lib.wf_pack_row_blocks.restype = ctypes.c_int
+    lib.wf_pack_row_blocks.argtypes = [_vp, _vp, _i64, _i64, _i64, _i64, _i32, _i64, _i64, _i32, _vp]
+    lib.wf_peer_pull_blocks.restype = ctypes.c_int
+    lib.wf_peer_pull_blocks.argtypes = [ctypes.POINTER(_vp), _i32, _i32, _i32, _i32, _i64, _i64, _i64, _i64, _vp,
+                                        ctypes.POINTER(_vp), _i32, ctypes.POINTER(_vp)]
     lib.wf_gather_rows_bench.restype = ctypes.c_int
     lib.wf_gather_rows_bench.argtypes = [_vp, _vp, _i64, _i64, _vp, _i64, _i32, _i64, _vp, _vp]
     lib.wf_testing_withhold_pair_arrive.restype = ctypes.c_int

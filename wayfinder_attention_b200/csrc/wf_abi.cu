@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 namespace {
@@ -145,6 +146,101 @@ int wf_gather_rows_bench(const void* k, const void* v, int64_t row_bytes, int64_
                                               static_cast<cudaStream_t>(stream));
   if (rc < 0) return fail(WF_ERR_UNSUPPORTED, "wf_gather_rows_bench: rows of 16..1024 bytes in 16-byte steps");
   if (rc) return cuda_fail(rc, "wf_gather_rows_bench");
+  return ok();
+}
+
+// ---------------------------------------------------------------- peer-memory K/V exchange
+// Buffers shared between the processes of one node through CUDA IPC, and the
+// copy-engine pulls of the sequence-sharded path (see include/wayfinder.h).
+
+int wf_peer_buffer_alloc(size_t bytes, void** ptr, void* handle_out) {
+  if (!ptr || !handle_out || bytes == 0) return fail(WF_ERR_INVALID_ARGUMENT, "wf_peer_buffer_alloc: bad argument");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail((int)e, "wf_peer_buffer_alloc: cudaMalloc");
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail((int)e, "wf_peer_buffer_alloc: cudaIpcGetMemHandle");
+  }
+  memcpy(handle_out, &h, sizeof(h));
+  *ptr = p;
+  return ok();
+}
+
+int wf_peer_buffer_free(void* ptr) {
+  if (!ptr) return ok();
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return cuda_fail((int)e, "wf_peer_buffer_free");
+  return ok();
+}
+
+int wf_peer_buffer_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return fail(WF_ERR_INVALID_ARGUMENT, "wf_peer_buffer_open: null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail((int)e, "wf_peer_buffer_open: cudaIpcOpenMemHandle");
+  return ok();
+}
+
+int wf_peer_buffer_close(void* ptr) {
+  if (!ptr) return ok();
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return cuda_fail((int)e, "wf_peer_buffer_close");
+  return ok();
+}
+
+int wf_pack_row_blocks(void* base, const void* src, int64_t B, int64_t Tl, int64_t row_bytes,
+                       int64_t src_batch_stride_bytes, int32_t chunks, int64_t chunk_stride, int64_t rank_stride,
+                       int32_t rank, void* stream) {
+  if (!base || !src || B < 1 || Tl < 1 || row_bytes < 1 || chunks < 1 || Tl % chunks)
+    return fail(WF_ERR_INVALID_ARGUMENT, "wf_pack_row_blocks: bad sizes (Tl must be a multiple of chunks)");
+  const int64_t tc = Tl / chunks;
+  const size_t width = (size_t)(tc * row_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int c = 0; c < chunks; ++c) {
+    char* dst = static_cast<char*>(base) + c * chunk_stride + (int64_t)rank * rank_stride;
+    const char* from = static_cast<const char*>(src) + c * tc * row_bytes;
+    const cudaError_t e = B == 1 ? cudaMemcpyAsync(dst, from, width, cudaMemcpyDeviceToDevice, st)
+                                 : cudaMemcpy2DAsync(dst, width, from, (size_t)src_batch_stride_bytes, width,
+                                                     (size_t)B, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return cuda_fail((int)e, "wf_pack_row_blocks");
+  }
+  return ok();
+}
+
+int wf_peer_pull_blocks(void* const* bases, int32_t world, int32_t rank, int32_t chunks, int32_t tensors,
+                        int64_t block_bytes, int64_t rank_stride, int64_t chunk_stride, int64_t tensor_stride,
+                        void* start_event, void* const* streams, int32_t n_streams, void* const* chunk_events) {
+  if (!bases || world < 1 || rank < 0 || rank >= world || chunks < 1 || tensors < 1 || block_bytes < 1 ||
+      !streams || n_streams < 1 || !chunk_events)
+    return fail(WF_ERR_INVALID_ARGUMENT, "wf_peer_pull_blocks: bad argument");
+  for (int p = 0; p < world; ++p)
+    if (!bases[p]) return fail(WF_ERR_INVALID_ARGUMENT, "wf_peer_pull_blocks: base of rank %d is NULL", p);
+  for (int s = 0; s < n_streams && s < chunks; ++s)
+    if (start_event) {
+      const cudaError_t e = cudaStreamWaitEvent(static_cast<cudaStream_t>(streams[s]),
+                                                static_cast<cudaEvent_t>(start_event), 0);
+      if (e != cudaSuccess) return cuda_fail((int)e, "wf_peer_pull_blocks: wait");
+    }
+  char* mine = static_cast<char*>(bases[rank]);
+  for (int c = 0; c < chunks; ++c) {
+    cudaStream_t st = static_cast<cudaStream_t>(streams[c % n_streams]);
+    // peers in rank order starting after this rank, so the ranks spread their pulls
+    for (int i = 1; i < world; ++i) {
+      const int p = (rank + i) % world;
+      for (int t = 0; t < tensors; ++t) {
+        const int64_t off = t * tensor_stride + c * chunk_stride + p * rank_stride;
+        const cudaError_t e = cudaMemcpyAsync(mine + off, static_cast<const char*>(bases[p]) + off,
+                                              (size_t)block_bytes, cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return cuda_fail((int)e, "wf_peer_pull_blocks: copy");
+      }
+    }
+    const cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(chunk_events[c]), st);
+    if (e != cudaSuccess) return cuda_fail((int)e, "wf_peer_pull_blocks: event");
+  }
   return ok();
 }
 

@@ -110,17 +110,29 @@ def chunked_kv_attention(q_l: torch.Tensor, idx: torch.Tensor, k_g: torch.Tensor
     t < K-1 point ahead) and ``wait(c)``, if given, is called before chunk c is
     enqueued — the caller makes the stream wait for that chunk's K/V there.
     """
+    C, W, B, Tc, H, D = k_g.shape
+    if tuple(v_g.shape) != tuple(k_g.shape) or not k_g.is_contiguous() or not v_g.is_contiguous():
+        raise ValueError(f"k_g / v_g must be contiguous chunk-major (C, W, B, Tc, H, D), got {tuple(k_g.shape)}")
+    return _chunked_attention(q_l, idx, k_g.data_ptr(), v_g.data_ptr(), (C, W, B, Tc, H, D), scale, tile, pad_mode,
+                              out_dtype, wait)
+
+
+def _chunked_attention(q_l, idx, k_base: int, v_base: int, shape, scale, tile, pad_mode, out_dtype, wait):
+    """``chunked_kv_attention`` on raw device addresses of contiguous (C, W, B, Tc, H, D) K/V buffers."""
+    import ctypes
+
     from . import _lib
 
-    C, W, B, Tc, H, D = k_g.shape
+    C, W, B, Tc, H, D = shape
     Tl = q_l.shape[2]
-    if Tl != C * Tc or tuple(v_g.shape) != tuple(k_g.shape) or q_l.shape[0] != B or q_l.shape[1] != H:
-        raise ValueError(f"q {tuple(q_l.shape)} does not match chunk-major K/V {tuple(k_g.shape)}")
+    if Tl != C * Tc or q_l.shape[0] != B or q_l.shape[1] != H or q_l.shape[3] != D:
+        raise ValueError(f"q {tuple(q_l.shape)} does not match chunk-major K/V {tuple(shape)}")
     T = W * Tl
     dev = q_l.device
     out = torch.empty(B, H, Tl, D, dtype=out_dtype or q_l.dtype, device=dev)
-    kb = k_g[0, 0].permute(0, 2, 1, 3)  # block (chunk 0, rank 0) as (B, H, Tc, D)
-    vb = v_g[0, 0].permute(0, 2, 1, 3)
+    # block (chunk 0, rank 0) as a (B, H, Tc, D) view of (B, Tc, H, D) memory
+    kv_strides = (ctypes.c_int64 * 4)(Tc * H * D, D, H * D, 1)
+    block = B * Tc * H * D
     K = idx.shape[-1]
     lib = _lib.load_library()
     flags = _lib.WF_ATTN_MASK_NEGATIVE if pad_mode == "masked" else 0
@@ -132,14 +144,121 @@ def chunked_kv_attention(q_l: torch.Tensor, idx: torch.Tensor, k_g: torch.Tensor
             rows = slice(c * Tc, (c + 1) * Tc)
             qc, ic, oc = q_l[:, :, rows], idx[:, rows], out[:, :, rows]
             rc = lib.wf_sparse_attention_cyclic_kv_chunked(
-                qc.data_ptr(), kb.data_ptr(), vb.data_ptr(), _lib.dtype_code(q_l.dtype), ic.data_ptr(),
-                B, H, Tc, T, D, K, _lib.strides(qc), _lib.strides(kb), _lib.strides(vb), _lib.strides(ic),
+                qc.data_ptr(), k_base, v_base, _lib.dtype_code(q_l.dtype), ic.data_ptr(),
+                B, H, Tc, T, D, K, _lib.strides(qc), kv_strides, kv_strides, _lib.strides(ic),
                 float(scale), flags, oc.data_ptr(), _lib.dtype_code(out.dtype), _lib.strides(oc),
-                tile, W, Tc, k_g.stride(1), v_g.stride(1), st, _lib.stream_ptr(dev),
+                tile, W, Tc, block, block, st, _lib.stream_ptr(dev),
             )
             _lib.check(rc)
     _lib.status_after(dev, None)
     return out
+
+
+class _PeerKV:
+    """Chunk-major K/V gather buffer shared through CUDA IPC, filled by copy-engine pulls.
+
+    Layout (2, C, W, B, Tc, H, D): tensor 0 is K, 1 is V; block (c, w) holds rank w's
+    local rows [c*Tc, (c+1)*Tc).  Every rank packs its own blocks, then pulls the
+    other ranks' blocks straight from their buffers over NVLink (``wf_peer_pull_blocks``).
+    Two one-element all-reduces order the exchange across ranks: before packing
+    (every peer has finished pulling the previous call's blocks) and before pulling
+    (every peer has packed this call's).
+    """
+
+    def __init__(self, shape, dtype: torch.dtype, dev: torch.device, group, n_streams: int = 2):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self.shape = tuple(shape)
+        self.dtype = dtype
+        self.dev = dev
+        self.group = group
+        C, W, B, Tc, H, D = self.shape
+        self.esz = torch.empty((), dtype=dtype).element_size()
+        self.block = B * Tc * H * D * self.esz
+        self.nbytes = 2 * C * W * self.block
+        lib = _lib.load_library()
+        self.lib = lib
+        self.rank = dist.get_rank(group)
+        self.world = W
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        with torch.cuda.device(dev):
+            _lib.check(lib.wf_peer_buffer_alloc(self.nbytes, ctypes.byref(ptr), handle))
+        self.own = ptr.value
+        handles = [None] * W
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.bases = (ctypes.c_void_p * W)()
+        self.opened = []
+        with torch.cuda.device(dev):
+            for p in range(W):
+                if p == self.rank:
+                    self.bases[p] = self.own
+                    continue
+                hp = (ctypes.c_uint8 * 64).from_buffer_copy(handles[p])
+                peer = ctypes.c_void_p()
+                _lib.check(lib.wf_peer_buffer_open(hp, ctypes.byref(peer)))
+                self.bases[p] = peer.value
+                self.opened.append(peer.value)
+        self.streams = [torch.cuda.Stream(device=dev) for _ in range(max(1, min(n_streams, C)))]
+        self.stream_ptrs = (ctypes.c_void_p * len(self.streams))(*[s.cuda_stream for s in self.streams])
+        self.events = [torch.cuda.Event() for _ in range(C)]
+        cur = torch.cuda.current_stream(dev)
+        for e in self.events:  # create the CUDA events (torch creates them at the first record)
+            e.record(cur)
+        self.event_ptrs = (ctypes.c_void_p * C)(*[e.cuda_event for e in self.events])
+        self.start = torch.cuda.Event()
+        self.start.record(cur)
+        self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    @property
+    def k_base(self) -> int:
+        return self.own
+
+    @property
+    def v_base(self) -> int:
+        C, W = self.shape[0], self.shape[1]
+        return self.own + C * W * self.block
+
+    def exchange(self, kt: torch.Tensor, vt: torch.Tensor, side: torch.cuda.Stream) -> None:
+        """Pack this rank's (B, Tl, H, D) K/V rows and enqueue the pulls (on ``side`` and the copy streams)."""
+        import torch.distributed as dist
+
+        from . import _lib
+
+        C, W, B, Tc, H, D = self.shape
+        with torch.cuda.stream(side):
+            for e in self.events:  # this rank's pulls of the previous call have landed
+                side.wait_event(e)
+            dist.all_reduce(self.flag, group=self.group)  # ... and every peer's: safe to overwrite own blocks
+            for t, x in ((0, kt), (1, vt)):
+                if x.stride(3) != 1 or x.stride(2) != D or x.stride(1) != H * D:
+                    x = x.contiguous()
+                _lib.check(self.lib.wf_pack_row_blocks(
+                    self.own + t * C * W * self.block, x.data_ptr(), B, C * Tc, H * D * self.esz,
+                    x.stride(0) * self.esz, C, W * self.block, self.block, self.rank, side.cuda_stream))
+            dist.all_reduce(self.flag, group=self.group)  # every rank's own blocks are packed
+            self.start.record(side)
+        _lib.check(self.lib.wf_peer_pull_blocks(
+            self.bases, W, self.rank, C, 2, self.block, self.block, W * self.block, C * W * self.block,
+            self.start.cuda_event, self.stream_ptrs, len(self.streams), self.event_ptrs))
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective: every rank calls it)."""
+        import torch.distributed as dist
+
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)  # no rank still pulls
+        for p in self.opened:
+            self.lib.wf_peer_buffer_close(p)
+        self.opened = []
+        dist.barrier(group=self.group)  # every rank has unmapped this rank's buffer
+        if self.own:
+            self.lib.wf_peer_buffer_free(self.own)
+            self.own = None
 
 
 class SequenceShardedAttention:
@@ -162,27 +281,44 @@ class SequenceShardedAttention:
     """
 
     def __init__(self, top_k: int, scale: float, tile: int = 256, group=None, pad_mode: str = "reference",
-                 chunks: int | None = None):
+                 chunks: int | None = None, transport: str = "peer"):
+        if transport not in ("peer", "nccl"):
+            raise ValueError(f"transport must be 'peer' or 'nccl', got {transport!r}")
         self.top_k = top_k
         self.scale = scale
         self.tile = tile
         self.group = group
         self.pad_mode = pad_mode
         self.chunks = chunks
+        self.transport = transport
         # persistent per-shape gather buffers and side stream: a forward allocates nothing large
         self._kg = None
         self._vg = None
+        self._peer = None
         self._side = None
 
     def _n_chunks(self, Tl: int, world: int) -> int:
-        # Default: one chunk on 2 ranks, where retrieval already hides the gather
+        # NCCL transport: one chunk on 2 ranks, where retrieval already hides the gather
         # (cfg4: 9.38 ms unchunked, 9.55 ms in 8 chunks), 8 chunks from 4 ranks up,
         # where each rank receives (W-1)/W of K/V while its retrieval shrinks as 1/W.
-        want = self.chunks if self.chunks is not None else (1 if world <= 2 else 8)
+        # Peer transport: 2 chunks (copy-engine pulls run beside the kernels; fewer,
+        # larger attention launches lose less to launch tails).
+        if self.chunks is not None:
+            want = self.chunks
+        elif self.transport == "peer":
+            want = 1 if world <= 2 else 2
+        else:
+            want = 1 if world <= 2 else 8
         c = max(1, min(want, 64 // world, Tl // self.tile))
         while c > 1 and Tl % (c * self.tile):
             c -= 1
         return c
+
+    def close(self) -> None:
+        """Release the peer buffers (collective: every rank of the group calls it)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     def forward(self, q_addr_l: torch.Tensor, k_addr_l: torch.Tensor, q_l: torch.Tensor, k_l: torch.Tensor,
                 v_l: torch.Tensor, out_dtype: torch.dtype | None = None) -> tuple[torch.Tensor, torch.Tensor]:
@@ -196,20 +332,33 @@ class SequenceShardedAttention:
             raise ValueError(f"top_k={self.top_k} must not exceed the row tile {self.tile}")
         C = self._n_chunks(Tl, world)
         Tc = Tl // C
-        main = torch.cuda.current_stream(q_l.device)
-        if self._side is None or self._side.device != q_l.device:
-            self._side = torch.cuda.Stream(device=q_l.device)
+        dev = q_l.device
+        main = torch.cuda.current_stream(dev)
+        if self._side is None or self._side.device != dev:
+            self._side = torch.cuda.Stream(device=dev)
         side = self._side
         shape = (C, world, B, Tc, H, D)
         kt, vt = k_l.transpose(1, 2), v_l.transpose(1, 2)  # (B, Tl, H, D)
-        if self._kg is None or tuple(self._kg.shape) != shape or self._kg.dtype != k_l.dtype or self._kg.device != k_l.device:
-            self._kg = torch.empty(shape, dtype=k_l.dtype, device=k_l.device)
-            self._vg = torch.empty(shape, dtype=v_l.dtype, device=v_l.device)
-        k_g, v_g = self._kg, self._vg
         # The key addresses (small) go first: collectives of one process group run in
-        # issue order, so issued after the K/V chunks the retrieval would wait for them.
+        # issue order, so issued after the K/V exchange the retrieval would wait for it.
         k_addr = gather_sequence(k_addr_l, self.tile, self.group)  # reordered to global order
         side.wait_stream(main)  # the previous call's attention has finished with the buffers
+        if self.transport == "peer":
+            if self._peer is None or self._peer.shape != shape or self._peer.dtype != k_l.dtype:
+                self.close()
+                self._peer = _PeerKV(shape, k_l.dtype, dev, self.group)
+            peer = self._peer
+            peer.exchange(kt, vt, side)
+            idx = sharded_causal_topk(q_addr_l, k_addr, self.top_k, world, rank, self.tile, self.pad_mode)
+            out = _chunked_attention(q_l, idx, peer.k_base, peer.v_base, shape, self.scale, self.tile,
+                                     self.pad_mode, out_dtype,
+                                     wait=lambda c: [main.wait_event(e) for e in (peer.events[c:c + 1] if c
+                                                                                  else peer.events)])
+            return out, idx
+        if self._kg is None or tuple(self._kg.shape) != shape or self._kg.dtype != k_l.dtype or self._kg.device != dev:
+            self._kg = torch.empty(shape, dtype=k_l.dtype, device=dev)
+            self._vg = torch.empty(shape, dtype=v_l.dtype, device=dev)
+        k_g, v_g = self._kg, self._vg
         landed = []
         with torch.cuda.stream(side):
             for c in range(C):
