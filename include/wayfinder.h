@@ -322,9 +322,11 @@ WF_API int wf_sparse_attention_backward(const void* q, const void* k, const void
  *                          stride src_batch_stride_bytes) into blocks (c, rank) of a
  *                          chunk-major buffer: block (c, r) of Tl/chunks rows per batch
  *                          element at base + c*chunk_stride + r*rank_stride
- *   wf_peer_pull_blocks  : for every chunk c, copy blocks (c, p) of every tensor t from
- *                          each peer p's buffer (bases[p], mapped) into the same place of
- *                          bases[rank]; chunk c's copies go to streams[c % n_streams],
+ *   wf_peer_pull_blocks  : for every chunk c in increasing order, copy blocks (c, p) of
+ *                          every tensor t from each peer p's buffer (bases[p], mapped) into
+ *                          the same place of bases[rank]; chunk c's copies go to
+ *                          streams[c % n_streams] (with one stream, chunk_events[c] also
+ *                          marks every earlier chunk),
  *                          which first wait start_event (NULL: none), and chunk_events[c]
  *                          is recorded after them.  The caller orders the pulls after every
  *                          rank packed its blocks, and its next pack after every rank's

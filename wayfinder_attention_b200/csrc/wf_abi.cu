@@ -226,6 +226,7 @@ int wf_peer_pull_blocks(void* const* bases, int32_t world, int32_t rank, int32_t
       if (e != cudaSuccess) return cuda_fail((int)e, "wf_peer_pull_blocks: wait");
     }
   char* mine = static_cast<char*>(bases[rank]);
+  // chunks in order: the attention of query chunk c reads key chunks <= c
   for (int c = 0; c < chunks; ++c) {
     cudaStream_t st = static_cast<cudaStream_t>(streams[c % n_streams]);
     // peers in rank order starting after this rank, so the ranks spread their pulls

@@ -165,7 +165,7 @@ class _PeerKV:
     (every peer has packed this call's).
     """
 
-    def __init__(self, shape, dtype: torch.dtype, dev: torch.device, group, n_streams: int = 2):
+    def __init__(self, shape, dtype: torch.dtype, dev: torch.device, group, n_streams: int = 1):
         import ctypes
 
         import torch.distributed as dist
@@ -301,12 +301,13 @@ class SequenceShardedAttention:
         # NCCL transport: one chunk on 2 ranks, where retrieval already hides the gather
         # (cfg4: 9.38 ms unchunked, 9.55 ms in 8 chunks), 8 chunks from 4 ranks up,
         # where each rank receives (W-1)/W of K/V while its retrieval shrinks as 1/W.
-        # Peer transport: 2 chunks (copy-engine pulls run beside the kernels; fewer,
-        # larger attention launches lose less to launch tails).
+        # Peer transport: one chunk on 2 ranks (the pulls hide behind retrieval), 4 from
+        # 4 ranks up: the pulls land chunk by chunk, in order, on one copy stream, so
+        # the attention of a chunk starts while later chunks arrive.
         if self.chunks is not None:
             want = self.chunks
         elif self.transport == "peer":
-            want = 1 if world <= 2 else 2
+            want = 1 if world <= 2 else 4
         else:
             want = 1 if world <= 2 else 8
         c = max(1, min(want, 64 // world, Tl // self.tile))
@@ -352,7 +353,7 @@ class SequenceShardedAttention:
             idx = sharded_causal_topk(q_addr_l, k_addr, self.top_k, world, rank, self.tile, self.pad_mode)
             out = _chunked_attention(q_l, idx, peer.k_base, peer.v_base, shape, self.scale, self.tile,
                                      self.pad_mode, out_dtype,
-                                     wait=lambda c: [main.wait_event(e) for e in (peer.events[c:c + 1] if c
+                                     wait=lambda c: [main.wait_event(e) for e in (peer.events[:c + 1] if c
                                                                                   else peer.events)])
             return out, idx
         if self._kg is None or tuple(self._kg.shape) != shape or self._kg.dtype != k_l.dtype or self._kg.device != dev:
