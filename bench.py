@@ -43,8 +43,9 @@ L2_FLUSH_BYTES = 256 << 20
 METRIC = "fused top-K+sparse-attn fwd queries/s @T=16K,K=128"
 # dram__bytes_read.sum + dram__bytes_write.sum of one sparse-attention launch: constants
 # from the named ncu captures (not measured in this run).
-ATTN_DRAM_BYTES = {"cfg2": 62.3e6}
-ATTN_DRAM_SOURCE = {"cfg2": "profiles/sparse_attention_cfg2.md"}
+ATTN_DRAM_BYTES = {"cfg2": 62.0e6, "cfg4": 7.89e9 + 0.54e9, "cfg5": 3.48e9 + 1.06e9}
+ATTN_DRAM_SOURCE = {"cfg2": "profiles/sparse_attention_cfg2.md", "cfg4": "profiles/sparse_attention_cfg4_cfg5.md",
+                    "cfg5": "profiles/sparse_attention_cfg4_cfg5.md"}
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -307,6 +308,7 @@ def main() -> None:
     topk_tot = sum(e[0].elapsed_time(e[1]) for e in kev)
     attn_tot = sum(e[1].elapsed_time(e[2]) for e in kev)
     ceiling_gbs = gather_ceiling(x, idx, args.steps, flush, stream)
+    bulk = bulk_gather_rates(x, idx, args.steps, flush, stream)
     t = torch.tensor([total_ms, topk_tot, attn_tot], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -393,12 +395,29 @@ def main() -> None:
     # the one data path with a collective: cfg4's long sequence over all ranks, and the
     # same call on one GPU (rank 0, the others wait) for the strong-scaling efficiency
     seq = None
+    batch_sharded = {}
     if world > 1 and not args.no_extra_configs:
         seq = sequence_sharded_measure(CONFIGS["cfg4"], rank, world, dev, max(3, args.steps // 4), 3)
         if rank == 0:
             one = config_measurement("cfg4", dev, flush, max(3, args.steps // 4))
             seq["single_gpu_ms"] = one["ms"]
             seq["strong_scaling_efficiency"] = one["ms"] / (world * seq["ms"])
+        dist.barrier()
+        # batch-sharded configs: cfg5 (B=64, K=128) and the cfg3 decoder (B=8), each rank
+        # its share of the batch, no collective; the job time is the slowest rank's
+        w5 = CONFIGS["cfg5"]
+        if w5.B % world == 0:
+            m5 = config_measurement("cfg5", dev, flush, 3, B=w5.B // world, seed=45 + rank)
+            t5 = torch.tensor([m5["ms"]], dtype=torch.float64, device=dev)
+            dist.all_reduce(t5, op=dist.ReduceOp.MAX)
+            batch_sharded["cfg5_k128"] = {"ms": t5.item(), "B_per_rank": w5.B // world,
+                                          "queries_per_s": w5.B * w5.T / (t5.item() / 1e3)}
+        if 8 % world == 0 and not args.no_decoder:
+            d3 = decoder_forward(8 // world, 4096, flush, 5, dev)
+            t3 = torch.tensor([d3["ms"]], dtype=torch.float64, device=dev)
+            dist.all_reduce(t3, op=dist.ReduceOp.MAX)
+            batch_sharded["cfg3_decoder"] = {"ms": t3.item(), "B_per_rank": 8 // world,
+                                             "tokens_per_s": 8 * 4096 / (t3.item() / 1e3)}
         dist.barrier()
 
     result = None
@@ -440,7 +459,9 @@ def main() -> None:
                          "hbm": {"achieved": (dram / (attn_ms_launch / 1e3) / 1e9) if dram else None, "peak": hbm,
                                  "frac": (dram / (attn_ms_launch / 1e3) / 1e9 / hbm) if dram else None,
                                  "peak_kind": peak_kind},
-                         "note": "achieved = gathered K/V bytes (2*B*H*T*K*D*2) / kernel time"},
+                         "alternative_bulk_copy": bulk,
+                         "note": "achieved = gathered K/V bytes (2*B*H*T*K*D*2) / kernel time; "
+                                 "alternative_bulk_copy: the same rows through cp.async.bulk into shared memory"},
             "path_roofline": {"roofline_ms": roof_l2_s * 1e3, "frac": roof_l2_s * 1e3 / ms_per_step,
                               "score_tflops_achieved": w.score_flops() / (topk_ms_launch / 1e3) / 1e12,
                               "definition": "max(score FLOPs / bf16 peak, gathered bytes / measured gather "
@@ -474,12 +495,16 @@ def main() -> None:
             }
         if seq is not None:
             result["cfg4_sequence_sharded"] = seq
+        if batch_sharded:
+            result["batch_sharded"] = batch_sharded
         if world == 1 and not args.no_extra_configs:
             result["overlap_probe"] = overlap_probe(w, dev, flush, args.steps)
         if world == 1 and not args.no_extra_configs:
             # configurations whose K/V outgrow the 126 MB L2 (cfg4: 1.07 GB; cfg5: 2.1 GB per call)
             result["cfg4_single_gpu"] = config_measurement("cfg4", dev, flush, max(3, args.steps // 4))
-            result["cfg5_k128"] = config_measurement("cfg5", dev, flush, max(3, args.steps // 4))
+            for name in ("cfg5_k64", "cfg5", "cfg5_k256"):
+                result[name.replace("cfg5", "cfg5_k128") if name == "cfg5" else name] = config_measurement(
+                    name, dev, flush, 3)
         if world == 1 and not args.no_cpu_baseline:
             secs, n = time_cpu_oracle(w, host, args.cpu_baseline_rows)
             result["cpu_baseline"] = {
@@ -752,13 +777,43 @@ def gather_ceiling(x: dict, idx: torch.Tensor, steps: int, flush: torch.Tensor, 
     return 2.0 * B * T * K * H * D * esz / (ms / 1e3) / 1e9
 
 
-def config_measurement(name: str, dev, flush: torch.Tensor, steps: int) -> dict:
-    """One more configuration on this GPU (fused step and its two kernels), for configs beyond cfg2."""
+def bulk_gather_rates(x: dict, idx: torch.Tensor, steps: int, flush: torch.Tensor, stream) -> dict:
+    """GB/s of the same gather through cp.async.bulk into shared memory, without and with read-back."""
+    from wayfinder_attention_b200 import _lib
+
+    lib = _lib.load_library()
+    k, v = x["k"], x["v"]
+    B, H, T, D = k.shape
+    esz = k.element_size()
+    if H * D * esz != 1024:
+        return {}
+    sink = torch.empty(B * T, dtype=torch.int32, device=k.device)
+    K = idx.shape[-1]
+    res = {}
+    for name, rb in (("bulk_copy_only_gbs", 0), ("bulk_copy_and_read_gbs", 1)):
+        def run():
+            for b in range(B):
+                _lib.check(lib.wf_gather_rows_bulk_bench(k[b].data_ptr(), v[b].data_ptr(), k.stride(2) * esz,
+                                                         idx[b].data_ptr(), T, K, T, rb, sink[b * T:].data_ptr(),
+                                                         stream.cuda_stream))
+
+        for _ in range(3):
+            run()
+        ms = time_events(run, steps, flush, stream)
+        res[name] = 2.0 * B * T * K * H * D * esz / (ms / 1e3) / 1e9
+    return res
+
+
+def config_measurement(name: str, dev, flush: torch.Tensor, steps: int, B: int | None = None,
+                       seed: int = 45) -> dict:
+    """One more configuration on this GPU (fused step and its two kernels), for configs beyond cfg2.
+
+    ``B`` overrides the batch (a rank's share of a batch-sharded config)."""
     from wayfinder_attention_b200.causal_topk import _launch_topk
     from wayfinder_attention_b200.fused_sparse import _launch_attention, fused_sparse_attention
 
-    w = CONFIGS[name]
-    x = device_inputs(w, dev)
+    w = CONFIGS[name] if B is None else scaled(CONFIGS[name], B=B)
+    x = device_inputs(w, dev, seed)
     stream = torch.cuda.current_stream(dev)
     scale = w.D ** -0.5
     idx = torch.empty(w.B, w.T, min(w.K, w.T), dtype=torch.int32, device=dev)

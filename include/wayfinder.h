@@ -354,6 +354,13 @@ WF_API int wf_peer_pull_blocks(void* const* bases, int32_t world, int32_t rank, 
 WF_API int wf_gather_rows_bench(const void* k, const void* v, int64_t row_bytes, int64_t row_stride_bytes,
                                 const int32_t* idx, int64_t n_query, int32_t K, int64_t n_rows, uint32_t* sink,
                                 void* stream);
+/* The same gather with 1 KB rows moved by the bulk-copy engine (cp.async.bulk, global
+ * to shared, two-stage ring per warp), each row read back from shared memory with
+ * 16-byte loads when read_back != 0: the alternative to loading rows into registers.
+ * K a multiple of 4.  A query whose wait gave up gets 0xffffffff in sink. */
+WF_API int wf_gather_rows_bulk_bench(const void* k, const void* v, int64_t row_stride_bytes, const int32_t* idx,
+                                     int64_t n_query, int32_t K, int64_t n_rows, int32_t read_back, uint32_t* sink,
+                                     void* stream);
 
 /*
  * Test hook, no counterpart in the reference: makes the next tensor-core retrieval

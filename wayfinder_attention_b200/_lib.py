@@ -51,6 +51,7 @@ EXPORTED_SYMBOLS = (
     "wf_causal_topk_noalloc",
     "wf_testing_withhold_pair_arrive",
     "wf_gather_rows_bench",
+    "wf_gather_rows_bulk_bench",
     "wf_peer_buffer_alloc",
     "wf_peer_buffer_free",
     "wf_peer_buffer_open",
@@ -95,6 +96,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.wf_peer_pull_blocks.restype = ctypes.c_int
     lib.wf_peer_pull_blocks.argtypes = [ctypes.POINTER(_vp), _i32, _i32, _i32, _i32, _i64, _i64, _i64, _i64, _vp,
                                         ctypes.POINTER(_vp), _i32, ctypes.POINTER(_vp)]
+    lib.wf_gather_rows_bulk_bench.restype = ctypes.c_int
+    lib.wf_gather_rows_bulk_bench.argtypes = [_vp, _vp, _i64, _vp, _i64, _i32, _i64, _i32, _vp, _vp]
     lib.wf_gather_rows_bench.restype = ctypes.c_int
     lib.wf_gather_rows_bench.argtypes = [_vp, _vp, _i64, _i64, _vp, _i64, _i32, _i64, _vp, _vp]
     lib.wf_testing_withhold_pair_arrive.restype = ctypes.c_int

@@ -245,6 +245,19 @@ int wf_peer_pull_blocks(void* const* bases, int32_t world, int32_t rank, int32_t
   return ok();
 }
 
+int wf_gather_rows_bulk_bench(const void* k, const void* v, int64_t row_stride_bytes, const int32_t* idx,
+                              int64_t n_query, int32_t K, int64_t n_rows, int32_t read_back, uint32_t* sink,
+                              void* stream) {
+  if (!k || !v || !idx || !sink) return fail(WF_ERR_INVALID_ARGUMENT, "wf_gather_rows_bulk_bench: null pointer");
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) % 16)
+    return fail(WF_ERR_INVALID_ARGUMENT, "wf_gather_rows_bulk_bench: rows must be 16-byte aligned");
+  const int rc = wf::launch_gather_rows_bulk_bench(k, v, row_stride_bytes, idx, n_query, K, n_rows, read_back, sink,
+                                                   static_cast<cudaStream_t>(stream));
+  if (rc < 0) return fail(WF_ERR_UNSUPPORTED, "wf_gather_rows_bulk_bench: K must be a multiple of 4");
+  if (rc) return cuda_fail(rc, "wf_gather_rows_bulk_bench");
+  return ok();
+}
+
 int wf_testing_withhold_pair_arrive(int32_t round, uint64_t wait_limit_ns) {
   wf::topk_tc_test_withhold(round, wait_limit_ns);
   return ok();

@@ -9,6 +9,7 @@
 // folded into one word per warp so the loads stay live), so its rate is the
 // ceiling the attention kernel can approach with this load scheme.
 #include "wf_kernels.h"
+#include "wf_sm100.cuh"
 
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -61,7 +62,96 @@ __global__ void __launch_bounds__(kWarps * 32) gather_rows_kernel(const uint4* _
   if (lane == 0) sink[qi] = acc;
 }
 
+// The alternative the attention kernel does not use: the same rows moved by the
+// bulk-copy engine (cp.async.bulk, global -> shared, completion on an mbarrier).
+// One warp per query; lane 0 issues the K and V rows of kBulkKeys keys per stage
+// into a two-stage ring of this warp's shared memory and the warp waits for each
+// stage (bounded).  READ: the warp then reads every staged byte back with 16-byte
+// shared loads, as a kernel consuming the rows would; otherwise it reads nothing.
+constexpr int kBulkWarps = 4;
+constexpr int kBulkKeys = 4;
+constexpr int kBulkStage = 2 * kBulkKeys * 1024;  // K and V rows of kBulkKeys keys
+constexpr uint64_t kBulkWaitNs = 1000000000ull;
+
+template <bool READ>
+__global__ void __launch_bounds__(kBulkWarps * 32) gather_rows_bulk_kernel(const char* __restrict__ k,
+                                                                         const char* __restrict__ v,
+                                                                         int64_t stride_bytes,
+                                                                         const int32_t* __restrict__ idx,
+                                                                         int64_t n_query, int K, int64_t n_rows,
+                                                                         uint32_t* __restrict__ sink) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t bars[kBulkWarps][2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t qi = (int64_t)blockIdx.x * kBulkWarps + warp;
+  unsigned char* ring = smem + (size_t)warp * 2 * kBulkStage;
+  if (lane == 0) {
+    sm100::mbar_init(&bars[warp][0], 1);
+    sm100::mbar_init(&bars[warp][1], 1);
+    sm100::fence_mbarrier_init();
+  }
+  __syncwarp();
+  if (qi >= n_query) return;
+  const int32_t* row = idx + qi * K;
+  const int nchunk = K / kBulkKeys;
+  auto issue = [&](int ch) {
+    if (lane != 0) return;
+    uint64_t* bar = &bars[warp][ch & 1];
+    unsigned char* dst = ring + (ch & 1) * kBulkStage;
+    sm100::mbar_arrive_expect_tx(bar, kBulkStage);
+    for (int u = 0; u < kBulkKeys; ++u) {
+      int j = row[ch * kBulkKeys + u];
+      j = (j >= 0 && j < n_rows) ? j : 0;
+      const char* srcs[2] = {k + (int64_t)j * stride_bytes, v + (int64_t)j * stride_bytes};
+      for (int t = 0; t < 2; ++t)
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                sm100::smem_u32(dst + (2 * u + t) * 1024)),
+            "l"(srcs[t]), "r"(1024), "r"(sm100::smem_u32(bar))
+            : "memory");
+    }
+  };
+  uint32_t acc = 0;
+  bool ok = true;
+  issue(0);
+  for (int ch = 0; ch < nchunk; ++ch) {
+    if (ch + 1 < nchunk) issue(ch + 1);  // the other stage was consumed in iteration ch - 1
+    ok = __all_sync(0xffffffffu, sm100::mbar_wait(&bars[warp][ch & 1], (uint32_t)(ch >> 1) & 1u, kBulkWaitNs));
+    if (!ok) {
+      // give the copies in flight (stages ch and ch + 1) one more bounded wait, then stop
+      for (int c = ch; c <= ch + 1 && c < nchunk; ++c)
+        sm100::mbar_wait(&bars[warp][c & 1], (uint32_t)(c >> 1) & 1u, kBulkWaitNs);
+      break;
+    }
+    if (READ) {
+      const uint4* st = reinterpret_cast<const uint4*>(ring + (ch & 1) * kBulkStage);
+#pragma unroll
+      for (int i = 0; i < kBulkStage / 16 / 32; ++i) {
+        const uint4 x = st[i * 32 + lane];
+        acc ^= x.x ^ x.y ^ x.z ^ x.w;
+      }
+    }
+    __syncwarp();
+  }
+  acc = __reduce_xor_sync(0xffffffffu, acc);
+  if (lane == 0) sink[qi] = ok ? acc : 0xffffffffu;  // a wait that gave up marks the query
+}
+
 }  // namespace
+
+int launch_gather_rows_bulk_bench(const void* k, const void* v, int64_t stride_bytes, const int32_t* idx,
+                                  int64_t n_query, int K, int64_t n_rows, int read_back, uint32_t* sink,
+                                  cudaStream_t stream) {
+  if (K < kBulkKeys || K % kBulkKeys || n_query < 1 || stride_bytes % 16) return -1;
+  const unsigned blocks = (unsigned)((n_query + kBulkWarps - 1) / kBulkWarps);
+  const int smem = kBulkWarps * 2 * kBulkStage;
+  auto kern = read_back ? gather_rows_bulk_kernel<true> : gather_rows_bulk_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return (int)e;
+  kern<<<blocks, kBulkWarps * 32, smem, stream>>>(static_cast<const char*>(k), static_cast<const char*>(v),
+                                                   stride_bytes, idx, n_query, K, n_rows, sink);
+  return (int)cudaGetLastError();
+}
 
 int launch_gather_rows_bench(const void* k, const void* v, int64_t row_bytes, int64_t stride_bytes,
                              const int32_t* idx, int64_t n_query, int K, int64_t n_rows, uint32_t* sink,

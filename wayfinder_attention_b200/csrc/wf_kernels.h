@@ -133,5 +133,9 @@ int launch_sparse_attention_backward(AttnBwdParams p, void* ws, size_t ws_bytes,
 int launch_gather_rows_bench(const void* k, const void* v, int64_t row_bytes, int64_t stride_bytes,
                              const int32_t* idx, int64_t n_query, int K, int64_t n_rows, uint32_t* sink,
                              cudaStream_t stream);
+// The same 1 KB rows moved by cp.async.bulk into shared memory (read back or not).
+int launch_gather_rows_bulk_bench(const void* k, const void* v, int64_t stride_bytes, const int32_t* idx,
+                                  int64_t n_query, int K, int64_t n_rows, int read_back, uint32_t* sink,
+                                  cudaStream_t stream);
 
 }  // namespace wf
