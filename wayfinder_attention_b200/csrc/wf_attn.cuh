@@ -84,7 +84,12 @@ __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, in
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = p.K;
-  const int KP = K | 1;  // odd row stride: the heads' score rows fall in different banks
+  // Score row stride: with K a multiple of 32 and L >= 4 lanes per head, K + L puts
+  // the heads' rows L banks apart (conflict-free in phase 2) and 16-byte aligned, so
+  // phase 3 reads four probabilities (and both phases four indices) per access;
+  // otherwise an odd stride keeps the rows in different banks.
+  const bool vec = L >= 4 && (K & 31) == 0;
+  const int KP = vec ? K + L : (K | 1);
   int* sI = reinterpret_cast<int*>(smem_raw) + (size_t)warp * (K + HW * KP);
   float* sP = reinterpret_cast<float*>(sI + K);  // [HW][KP]
 
@@ -155,10 +160,16 @@ __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, in
   for (int k0 = 0; k0 < K; k0 += kU) {
     uint4 raw[kU][NV];
     int jj[kU];
+    if (vec) {
+      const int4 j4 = *reinterpret_cast<const int4*>(sI + k0);
+      jj[0] = j4.x; jj[1] = j4.y; jj[2] = j4.z; jj[3] = j4.w;
+    } else {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) jj[u] = (k0 + u < K) ? sI[k0 + u] : kMasked;
+    }
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
-      const int j = (k0 + u < K) ? sI[k0 + u] : kMasked;
-      jj[u] = j;
+      const int j = jj[u];
 #pragma unroll
       for (int v = 0; v < NV; ++v)
         raw[u][v] = (j >= 0 && hv) ? ldg16(kb + kv_row_offset<CYC>(p, j, p.kst, p.k_rank_stride) + v * L * VEC) : make_uint4(0, 0, 0, 0);
@@ -210,11 +221,24 @@ __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, in
   for (int k0 = 0; k0 < K; k0 += kU) {
     uint4 raw[kU][NV];
     float pw[kU];
+    int jj[kU];
+    if (vec) {
+      const int4 j4 = *reinterpret_cast<const int4*>(sI + k0);
+      const float4 p4 = *reinterpret_cast<const float4*>(myP + k0);
+      jj[0] = j4.x; jj[1] = j4.y; jj[2] = j4.z; jj[3] = j4.w;
+      pw[0] = p4.x; pw[1] = p4.y; pw[2] = p4.z; pw[3] = p4.w;
+    } else {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const bool in = k0 + u < K;
+        jj[u] = in ? sI[k0 + u] : kMasked;
+        pw[u] = in ? myP[k0 + u] : 0.f;
+      }
+    }
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const bool in = k0 + u < K;
-      const int j = in ? sI[k0 + u] : kMasked;
-      pw[u] = in ? myP[k0 + u] : 0.f;
+      const int j = jj[u];
       if (DROP && in) pw[u] *= dropout_scale(p.drop_seed, drow + (uint64_t)(k0 + u), p.drop_rate, inv_keep);
 #pragma unroll
       for (int v = 0; v < NV; ++v)
@@ -254,7 +278,8 @@ int launch_t(const AttnParams& p, cudaStream_t stream) {
   constexpr int L = D / E;
   constexpr int HW = 32 / L;
   const int ngroups = (p.H + HW - 1) / HW;
-  const size_t per_warp = ((size_t)p.K + (size_t)HW * (p.K | 1)) * sizeof(int);
+  const bool vec = L >= 4 && (p.K & 31) == 0;  // the kernel's score-row stride rule
+  const size_t per_warp = ((size_t)p.K + (size_t)HW * (vec ? p.K + L : (p.K | 1))) * sizeof(int);
   int wpb = (int)(kSmemBudget / per_warp);
   wpb = wpb < 1 ? 1 : (wpb > 8 ? 8 : wpb);
   const size_t smem = per_warp * wpb;
