@@ -86,7 +86,10 @@ __global__ void __launch_bounds__(256) attn_bwd_query_kernel(const AttnBwdParams
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = p.K;
-  const int KP = K | 1;
+  // As in the forward: with K a multiple of 32 and L >= 4, rows K + L apart are
+  // 16-byte aligned and bank-disjoint, and indices / coefficients are read 4 at a time.
+  const bool vec = L >= 4 && (K & 31) == 0;
+  const int KP = vec ? K + L : (K | 1);
   int* sI = reinterpret_cast<int*>(smem_raw) + (size_t)warp * (K + 2 * HW * KP);
   float* sP = reinterpret_cast<float*>(sI + K);  // [HW][KP] scores, then p
   float* sD = sP + HW * KP;                      // [HW][KP] dp, then scale * ds
@@ -94,10 +97,11 @@ __global__ void __launch_bounds__(256) attn_bwd_query_kernel(const AttnBwdParams
   const int ngroups = (p.H + HW - 1) / HW;
   const int64_t w = (int64_t)blockIdx.x * warps_per_block + warp;
   if (w >= (int64_t)p.B * p.Tq * ngroups) return;
-  const int hg = (int)(w % ngroups);
-  const int64_t bt = w / ngroups;
-  const int t = (int)(bt % p.Tq);
-  const int b = (int)(bt / p.Tq);
+  // one (batch element, head group) at a time, as in the forward (L2 locality at long T)
+  const int t = (int)(w % p.Tq);
+  const int64_t bg = w / p.Tq;
+  const int hg = (int)(bg % ngroups);
+  const int b = (int)(bg / ngroups);
   const int hl = lane / L, sub = lane % L;
   const int h = hg * HW + hl;
   const bool hv = h < p.H;
@@ -130,10 +134,16 @@ __global__ void __launch_bounds__(256) attn_bwd_query_kernel(const AttnBwdParams
     for (int k0 = 0; k0 < K; k0 += kUB) {
       uint4 raw[kUB][NV];
       int jj[kUB];
+      if (vec) {
+        const int4 j4 = *reinterpret_cast<const int4*>(sI + k0);
+        jj[0] = j4.x; jj[1] = j4.y; jj[2] = j4.z; jj[3] = j4.w;
+      } else {
+#pragma unroll
+        for (int u = 0; u < kUB; ++u) jj[u] = (k0 + u < K) ? sI[k0 + u] : kMaskedB;
+      }
 #pragma unroll
       for (int u = 0; u < kUB; ++u) {
-        const int j = (k0 + u < K) ? sI[k0 + u] : kMaskedB;
-        jj[u] = j;
+        const int j = jj[u];
 #pragma unroll
         for (int v = 0; v < NV; ++v)
           raw[u][v] = (j >= 0 && hv) ? ldg16(base + (int64_t)j * st + v * L * VEC) : make_uint4(0, 0, 0, 0);
@@ -213,11 +223,23 @@ __global__ void __launch_bounds__(256) attn_bwd_query_kernel(const AttnBwdParams
   for (int k0 = 0; k0 < K; k0 += kUB) {
     uint4 raw[kUB][NV];
     float cw[kUB];
+    int jj[kUB];
+    if (vec) {
+      const int4 j4 = *reinterpret_cast<const int4*>(sI + k0);
+      const float4 c4 = *reinterpret_cast<const float4*>(myD + k0);
+      jj[0] = j4.x; jj[1] = j4.y; jj[2] = j4.z; jj[3] = j4.w;
+      cw[0] = c4.x; cw[1] = c4.y; cw[2] = c4.z; cw[3] = c4.w;
+    } else {
+#pragma unroll
+      for (int u = 0; u < kUB; ++u) {
+        const bool in = k0 + u < K;
+        jj[u] = in ? sI[k0 + u] : kMaskedB;
+        cw[u] = in ? myD[k0 + u] : 0.f;
+      }
+    }
 #pragma unroll
     for (int u = 0; u < kUB; ++u) {
-      const bool in = k0 + u < K;
-      const int j = in ? sI[k0 + u] : kMaskedB;
-      cw[u] = in ? myD[k0 + u] : 0.f;
+      const int j = jj[u];
 #pragma unroll
       for (int v = 0; v < NV; ++v)
         raw[u][v] = (j >= 0 && hv) ? ldg16(kb + (int64_t)j * p.kst + v * L * VEC) : make_uint4(0, 0, 0, 0);
@@ -397,7 +419,8 @@ int launch_bwd_t(const AttnBwdParams& p, cudaStream_t stream) {
   constexpr int L = D / E;
   constexpr int HW = 32 / L;
   const int ngroups = (p.H + HW - 1) / HW;
-  const size_t per_warp = ((size_t)p.K + 2 * (size_t)HW * (p.K | 1)) * sizeof(int);
+  const bool vec = L >= 4 && (p.K & 31) == 0;  // the kernel's row-stride rule
+  const size_t per_warp = ((size_t)p.K + 2 * (size_t)HW * (vec ? p.K + L : (p.K | 1))) * sizeof(int);
   int wpb = (int)(kBwdSmemBudget / per_warp);
   wpb = wpb < 1 ? 1 : (wpb > 8 ? 8 : wpb);
   const size_t smem = per_warp * wpb;
