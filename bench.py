@@ -850,7 +850,8 @@ def config_measurement(name: str, dev, flush: torch.Tensor, steps: int, B: int |
     return res
 
 
-def decoder_forward(B: int, T: int, flush: torch.Tensor, steps: int, dev, attention_type: str = "learned_address") -> dict:
+def decoder_forward(B: int, T: int, flush: torch.Tensor, steps: int, dev, attention_type: str = "learned_address",
+                    graph: bool = True) -> dict:
     """Whole-model prefill forward of the reference's systems-benchmark model family
     (4 layers, d_model 256, 4 heads, FFN 1024, vocab 128, K 128; transformer.py:76-312)
     with this build's attention, bf16 weights, random init, uniform token ids."""
@@ -876,8 +877,18 @@ def decoder_forward(B: int, T: int, flush: torch.Tensor, steps: int, dev, attent
             torch.cuda.synchronize()
             tot += a.elapsed_time(b)
     ms = tot / steps
-    return {"ms": ms, "tokens_per_s": B * T / (ms / 1e3), "B": B, "T": T, "attention": attention_type,
-            "model": "4 layers, d_model 256, H 4, FFN 1024, vocab 128, K 128, bf16"}
+    res = {"ms": ms, "tokens_per_s": B * T / (ms / 1e3), "B": B, "T": T, "attention": attention_type,
+           "model": "4 layers, d_model 256, H 4, FFN 1024, vocab 128, K 128, bf16"}
+    if graph:
+        # the same forward replayed from a CUDA graph (wayfinder_attention_b200.CapturedForward)
+        from wayfinder_attention_b200 import CapturedForward
+
+        cap = CapturedForward(lambda x: m(x)["logits"], ids)
+        stream = torch.cuda.current_stream(dev)
+        for _ in range(3):
+            cap(ids)
+        res["graph_ms"] = time_events(lambda: cap(ids), steps, flush, stream)
+    return res
 
 
 def dense_baseline(w: Workload, x: dict, flush: torch.Tensor, steps: int) -> dict:

@@ -24,6 +24,7 @@ from .attention import (
 from .router import MultiScaleRouter, PerLayerRouter, RouterMLP
 from .causal_topk import causal_topk, causal_topk_available, promote_compute_dtype
 from .decoder import DenseSDPAAttention, TransformerBlock, TransformerLM
+from .graphs import CapturedForward
 from .host_pipeline import HostFusedSparseAttention, host_fused_sparse_attention
 from .fused_sparse import (
     SparseMeatConfig,
@@ -42,6 +43,7 @@ __all__ = [
     "fused_sparse_attention_available",
     "sparse_meat_attention",
     "HostFusedSparseAttention",
+    "CapturedForward",
     "host_fused_sparse_attention",
     "SparseMeatConfig",
     "LearnedAddressModule",

@@ -236,7 +236,9 @@ def require_cuda(*tensors: torch.Tensor) -> torch.device:
 # then at most every READBACK_CALLS launches or READBACK_SECONDS, so the copy costs
 # nothing measurable — and a later call on the device raises ``RuntimeError`` once
 # that copy has landed.  ``check_status`` copies, waits and raises at once.  No
-# call synchronises the host except ``check_status``.
+# call synchronises the host except ``check_status``.  Launches captured into a CUDA
+# graph write the same word when the graph replays; it is read back by the next
+# eager call or by ``check_status``.
 
 STATUS_INDEX_OUT_OF_RANGE = 1
 STATUS_WAIT_TIMEOUT = 2
@@ -319,13 +321,14 @@ def status_arg(dev: torch.device, user: torch.Tensor | None):
             raise ValueError("status must be an int32 CUDA tensor")
         return user.data_ptr()
     st = _device_status(dev)
-    st.poll()
+    if not torch.cuda.is_current_stream_capturing():  # no event queries inside a graph capture
+        st.poll()
     return st.word.data_ptr()
 
 
 def status_after(dev: torch.device, user: torch.Tensor | None) -> None:
     """Queue the read-back of the internal status word after a launch that used it."""
-    if user is None:
+    if user is None and not torch.cuda.is_current_stream_capturing():
         _device_status(dev).after_launch()
 
 
