@@ -155,7 +155,9 @@ __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, in
   const TI* vb = reinterpret_cast<const TI*>(p.v) + (int64_t)b * p.vsb + (int64_t)hc * p.vsh + sub * VEC;
   float* myP = sP + hl * KP;
 
-  // Phase 1: scores.
+  // Phase 1: scores, and each head's running maximum (every lane of a head holds the
+  // reduced scores, so the maximum costs no pass over shared memory).
+  float m = -INFINITY;
 #pragma unroll 1
   for (int k0 = 0; k0 < K; k0 += kU) {
     uint4 raw[kU][NV];
@@ -186,19 +188,17 @@ __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, in
       }
 #pragma unroll
       for (int o = L / 2; o > 0; o >>= 1) d += __shfl_xor_sync(kFull, d, o);
-      if (sub == 0 && k0 + u < K) {
+      if (k0 + u < K) {
         const int j = jj[u];
-        myP[k0 + u] = j >= 0 ? d * p.scale : (j == kMasked ? -INFINITY : NAN);
+        const float sv = j >= 0 ? d * p.scale : (j == kMasked ? -INFINITY : NAN);
+        m = fmaxf(m, sv);  // a NaN score (bad index) leaves m alone; the sum below turns NaN
+        if (sub == 0) myP[k0 + u] = sv;
       }
     }
   }
   __syncwarp();
 
-  // Phase 2: softmax of each head over its K scores; the L lanes of a head share the work.
-  float m = -INFINITY;
-  for (int s = sub; s < K; s += L) m = fmaxf(m, myP[s]);
-#pragma unroll
-  for (int o = L / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+  // Phase 2: exponentials and their sum per head; the L lanes of a head share the work.
   float sum = 0.f;
   for (int s = sub; s < K; s += L) {
     const float x = myP[s];
