@@ -76,7 +76,8 @@ WF_API int wf_max_top_k(void);
  *             0 <= row_start < row_stride, and every g(l) < Tk.  This is how a rank of a
  *             query-row-sharded long sequence addresses its cyclic row blocks.
  *   idx_out : (B, Tq, K_eff) int32, contiguous.  Slots hold the retrieved key indices in
- *             descending score order; equal scores break to the lower index.
+ *             an unspecified (deterministic) order; equal scores break to the lower
+ *             index at the K-th place; pad slots come last.
  *   workspace, workspace_bytes: device scratch of at least wf_causal_topk_workspace_bytes();
  *             may be NULL/0 when that returns 0.
  *   status  : optional device int32; bit 1 is OR-ed in if a bounded internal wait of the

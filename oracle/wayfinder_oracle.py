@@ -16,11 +16,13 @@ It restates, in numpy fp32, the reference's own PyTorch path for
   sparse_meat_attention  <- sparse_meat_attention_reference      fused_sparse.py:80-94
     gather               <- _gather_kv_batched                    fused_sparse.py:64-77
 
-Two choices the reference leaves open are fixed here exactly as the CUDA
-kernels fix them: slots are sorted by descending score with ties broken to the
-lower key index (the reference's ``topk(sorted=False)`` order is
-implementation-defined), and the pad slots of rows i < K-1 are the trailing
-slots s = i+1 .. K-1 (the reference pads whichever slots topk left at -inf).
+Two choices the reference leaves open are fixed here: ties at the K-th score
+break to the lower key index (as in the CUDA kernels), slots are sorted by
+descending score (the reference's ``topk(sorted=False)`` order is
+implementation-defined, and so is the CUDA kernels' — comparisons are by index
+set), and the pad slots of rows i < K-1 are the trailing slots s = i+1 .. K-1
+(the reference pads whichever slots topk left at -inf; the CUDA kernels use the
+trailing slots too).
 
 Parity pin: ``tests/golden/`` holds outputs of the reference itself, produced
 by ``tests/golden/make_golden.py`` importing the reference in the build

@@ -69,6 +69,22 @@ def compare_indices(got: np.ndarray, want: np.ndarray, q_addr: np.ndarray, k_add
     return {"rows": B * n, "exempt": exempt, "bad": bad}
 
 
+def same_selection(got: np.ndarray, want: np.ndarray) -> bool:
+    """(..., T, K) index tensors select the same keys per row (in any slot order) and
+    agree exactly on the pad slots that follow the i + 1 keys of rows i < K-1."""
+    if got.shape != want.shape:
+        return False
+    T, K = got.shape[-2], got.shape[-1]
+    for i in range(T):
+        n = min(i + 1, K)
+        g, w = got[..., i, :], want[..., i, :]
+        if not (np.sort(g[..., :n], axis=-1) == np.sort(w[..., :n], axis=-1)).all():
+            return False
+        if not (g[..., n:] == w[..., n:]).all():
+            return False
+    return True
+
+
 def reference_pads(i: int, K: int, T: int) -> list[int]:
     """Pad indices of row i under the sorted-slot convention (causal_topk.py:37-57)."""
     return [(i + K + s + 1) % T for s in range(i + 1, K)]

@@ -182,10 +182,12 @@ def test_module_trains_with_attention_dropout(cuda_device):
     m = LearnedAddressSparseAttention(128, 2, top_k=16, dropout=0.1,
                                       retrieval_config={"use_fused_sparse": False}).to(cuda_device).train()
     x = torch.randn(2, 128, 128, device=cuda_device)
-    target = torch.randn(2, 128, 128, device=cuda_device)
-    opt = torch.optim.SGD(m.parameters(), lr=0.1)
+    # a target the layer can move toward quickly (its output norm), so the trend is
+    # far larger than the step-to-step noise of the dropout masks
+    target = torch.zeros(2, 128, 128, device=cuda_device)
+    opt = torch.optim.SGD(m.parameters(), lr=0.5)
     losses = []
-    for _ in range(4):
+    for _ in range(6):
         opt.zero_grad()
         loss = ((m(x) - target) ** 2).mean()
         loss.backward()

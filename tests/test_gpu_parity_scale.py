@@ -5,7 +5,7 @@ K in {64, 128, 256}, clustered addresses (the near-tie stress).  The oracle chec
 sampled rows (indices as sets with the near-tie exemption; attention within 2e-3
 on an fp32 output buffer, fed the kernel's own indices); every row of every batch
 element goes through the size-independent properties (causal, unique, no
-unretrieved key above a retrieved one, slots sorted by score).
+unretrieved key above a retrieved one).
 """
 
 import numpy as np

@@ -10,9 +10,9 @@ Output contract (identical to the reference's ``fused_causal`` path up to the
 order of slots inside a row):
   * ``(B, T, K_eff)`` int32 with ``K_eff = min(top_k, T)``;
   * row ``i`` holds the ``K_eff`` keys ``j <= i`` with the largest fp32 score
-    ``<q_i, k_j>``; here slots are sorted by descending score and equal
-    scores break to the lower key index (the reference leaves slot order to
-    ``torch.topk(sorted=False)``);
+    ``<q_i, k_j>`` (equal scores break to the lower key index); the order of
+    those keys within the row is unspecified, as the reference's
+    ``torch.topk(sorted=False)`` leaves it, but deterministic;
   * rows ``i < K_eff - 1`` have only ``i + 1`` causal keys; their remaining
     slots ``s`` hold the pad index ``(i + K_eff + s + 1) % T`` of
     ``_finalize_causal_topk`` (``causal_topk.py:37-57``), or ``-1`` with

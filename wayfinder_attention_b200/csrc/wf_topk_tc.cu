@@ -2,8 +2,10 @@
 //
 // Same contract as the CUDA-core kernel in wf_topk.cu (and the reference's
 // routing_attention/kernels/causal_topk.py:133-171 + :37-57): for every query
-// row g, the K keys j <= g with the largest fp32 score <q_g, k_j>, slots in
-// descending score order with ties to the lower index, pad slots for short rows.
+// row g, the K keys j <= g with the largest fp32 score <q_g, k_j> (ties to the
+// lower index), pad slots for short rows.  The order of the selected keys within
+// a row is unspecified (here: the candidate lists' order), as it is for the
+// reference's topk(sorted=False); the CUDA-core kernel happens to sort.
 //
 // Work split.  A tile of 128 query rows (the 128 TMEM lanes) is handled by a
 // cluster of two CTAs on two SMs; CTA rank r streams the key chunks c = r, r+2,
@@ -33,7 +35,7 @@
 //           is compacted to its exact top-K (warp radix select), which raises the
 //           row's admission threshold.  topk_finalize_kernel, launched right after
 //           at full occupancy (one warp per row), selects the exact top-K of the
-//           four lists, sorts it and writes the indices and pads.  Batches larger
+//           four lists and writes the indices and pads.  Batches larger
 //           than about 65536 query rows run in slices that reuse the workspace.
 // The margin, 2^-13 * sum_d |q_d| * max|k|, exceeds any plausible accumulation
 // error of a 32-term fp32 dot product with exact bf16/fp16 products, so every
@@ -53,7 +55,6 @@ namespace wf {
 namespace {
 
 using namespace sm100;
-using select::bitonic_sort_desc;
 using select::merge_row;
 using select::select_compact;
 
@@ -653,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------- finalisation
 // One warp per query row: the exact top-K of the two CTAs' candidate lists
 // (composites key << 32 | ~index, so larger = better and ties favour the lower
-// index), sorted descending, plus pad slots.  Runs at full occupancy; the
+// index), in list order, plus pad slots.  Runs at full occupancy; the
 // selection is the same warp radix select the streaming kernels use.
 struct FinParams {
   const uint64_t* ws;
@@ -716,20 +717,18 @@ __device__ __forceinline__ void finalize_row(const FinParams& p, int64_t row, co
     }
     e0 += take;
   } while (e0 < n);
-  uint64_t cc[SE];
-#pragma unroll
-  for (int t = 0; t < SE; ++t) {
-    const int e = t * 32 + lane;
-    cc[t] = (e < m) ? (((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e])) : 0ull;
-  }
-  bitonic_sort_desc<SE>(cc, lane);
+  // The selected keys go out in the order the lists hold them (admission order,
+  // compaction keeps it), not sorted by score: the reference leaves the slot order
+  // open too (topk(sorted=False)), and sorting cost a tenth of the retrieval.  The
+  // order is still a deterministic function of the inputs; pads take the trailing slots.
+  __syncwarp();
   int32_t* out = p.idx + row * p.K;
 #pragma unroll
   for (int t = 0; t < SE; ++t) {
     const int s = t * 32 + lane;
     if (s < p.K) {
       int val;
-      if (s < m) val = (int)(~(uint32_t)cc[t]);
+      if (s < m) val = bi[s];
       else val = p.pad_mode == 0 ? (int)(((int64_t)g + p.K + s + 1) % p.Tk) : -1;
       out[s] = val;
     }
