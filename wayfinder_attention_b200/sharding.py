@@ -106,9 +106,11 @@ def chunked_kv_attention(q_l: torch.Tensor, idx: torch.Tensor, k_g: torch.Tensor
     q_l: (B, H, Tl, D) this rank's rows (``local_rows`` order); idx: (B, Tl, K) global
     key indices; k_g, v_g: (C, W, B, Tc, H, D) with block (c, w) = rank w's local rows
     [c*Tc, (c+1)*Tc).  Chunk c of the query rows reads key chunks <= c only (causal),
-    so chunks run in the order 1..C-1, 0 (chunk 0 last: the reference pads of rows
-    t < K-1 point ahead) and ``wait(c)``, if given, is called before chunk c is
-    enqueued — the caller makes the stream wait for that chunk's K/V there.
+    so chunks run in order and ``wait(c, everything)``, if given, is called before
+    chunk c is enqueued — the caller makes the stream wait there for key chunks
+    0..c, or for all of them when ``everything`` is set.  That is the case for chunk
+    0 when the reference pads of rows t < K-1 (global rows up to 3K-2) may lie
+    beyond key chunk 0 (3K-2 >= Tc*W); chunk 0 then runs last.
     """
     C, W, B, Tc, H, D = k_g.shape
     if tuple(v_g.shape) != tuple(k_g.shape) or not k_g.is_contiguous() or not v_g.is_contiguous():
@@ -137,10 +139,12 @@ def _chunked_attention(q_l, idx, k_base: int, v_base: int, shape, scale, tile, p
     lib = _lib.load_library()
     flags = _lib.WF_ATTN_MASK_NEGATIVE if pad_mode == "masked" else 0
     st = _lib.status_arg(dev, None)
+    zero_last = 3 * K - 2 >= Tc * W
+    order = list(range(1, C)) + [0] if zero_last else list(range(C))
     with torch.cuda.device(dev):
-        for c in list(range(1, C)) + [0]:
+        for c in order:
             if wait is not None:
-                wait(c)
+                wait(c, c == 0 and zero_last)
             rows = slice(c * Tc, (c + 1) * Tc)
             qc, ic, oc = q_l[:, :, rows], idx[:, rows], out[:, :, rows]
             rc = lib.wf_sparse_attention_cyclic_kv_chunked(
@@ -353,8 +357,8 @@ class SequenceShardedAttention:
             idx = sharded_causal_topk(q_addr_l, k_addr, self.top_k, world, rank, self.tile, self.pad_mode)
             out = _chunked_attention(q_l, idx, peer.k_base, peer.v_base, shape, self.scale, self.tile,
                                      self.pad_mode, out_dtype,
-                                     wait=lambda c: [main.wait_event(e) for e in (peer.events[:c + 1] if c
-                                                                                  else peer.events)])
+                                     wait=lambda c, every: [main.wait_event(e) for e in
+                                                            (peer.events if every else peer.events[:c + 1])])
             return out, idx
         if self._kg is None or tuple(self._kg.shape) != shape or self._kg.dtype != k_l.dtype or self._kg.device != dev:
             self._kg = torch.empty(shape, dtype=k_l.dtype, device=dev)
@@ -371,7 +375,7 @@ class SequenceShardedAttention:
                 landed.append(ev)
         idx = sharded_causal_topk(q_addr_l, k_addr, self.top_k, world, rank, self.tile, self.pad_mode)
         out = chunked_kv_attention(q_l, idx, k_g, v_g, self.scale, self.tile, self.pad_mode, out_dtype,
-                                   wait=lambda c: main.wait_event(landed[c] if c else landed[-1]))
+                                   wait=lambda c, every: main.wait_event(landed[-1] if every else landed[c]))
         return out, idx
 
     __call__ = forward
