@@ -302,9 +302,10 @@ class SequenceShardedAttention:
         self._side = None
 
     def _n_chunks(self, Tl: int, world: int) -> int:
-        # NCCL transport: one chunk on 2 ranks, where retrieval already hides the gather
-        # (cfg4: 9.38 ms unchunked, 9.55 ms in 8 chunks), 8 chunks from 4 ranks up,
-        # where each rank receives (W-1)/W of K/V while its retrieval shrinks as 1/W.
+        # NCCL transport: one chunk on 2 ranks, where retrieval already hides the gather,
+        # 4 chunks from 4 ranks up, where each rank receives (W-1)/W of K/V while its
+        # retrieval shrinks as 1/W (cfg4 on 8 GPUs: 3.04 ms in 4 chunks, 3.10 in 2,
+        # 3.75 in 8: smaller all-gathers run at lower bandwidth).
         # Peer transport: one chunk on 2 ranks (the pulls hide behind retrieval), 4 from
         # 4 ranks up: the pulls land chunk by chunk, in order, on one copy stream, so
         # the attention of a chunk starts while later chunks arrive.
@@ -313,7 +314,7 @@ class SequenceShardedAttention:
         elif self.transport == "peer":
             want = 1 if world <= 2 else 4
         else:
-            want = 1 if world <= 2 else 8
+            want = 1 if world <= 2 else 4
         c = max(1, min(want, 64 // world, Tl // self.tile))
         while c > 1 and Tl % (c * self.tile):
             c -= 1
