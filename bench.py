@@ -485,7 +485,7 @@ def main() -> None:
                     "host_link_gbs_per_rank": (h2d + d2h) / (copy_ms / 1e3) / 1e9,
                     "frac_of_copy_ceiling": copy_ms / e2e_ms_step,
                     "note": "copies_only: the same uploads and downloads on every rank at once, no kernels"},
-            "gpu_launches": 3 * args.steps,  # per step: retrieval, finalisation, attention
+            "gpu_launches": 4 * args.steps,  # per step: scoring, rescoring, finalisation, attention
             "clocks": clk.summary(),
         }
         if not args.no_dense:
@@ -644,7 +644,7 @@ def run_sequence_sharded(args, w: Workload, rank: int, world: int, dev) -> None:
                        "l2": "flushed before every timed step"},
             "path_roofline": {"roofline_ms_per_gpu": roof_ms, "frac": roof_ms / ms, "peak_kind": peak_kind},
             "parts_ms": m["parts_ms"], "transport": m["transport"], "nccl_transport": m.get("nccl"),
-            "gpu_launches": (2 + m["chunks"]) * args.steps,  # per step: retrieval, finalisation, attention chunks
+            "gpu_launches": (3 + m["chunks"]) * args.steps,  # per step: scoring, rescoring, finalisation, attention chunks
             "clocks": m["clocks"],
         })
 

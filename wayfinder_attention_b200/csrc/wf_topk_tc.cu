@@ -25,18 +25,23 @@
 //           K-th best score; the two CTAs bisect it together (7 steps, counts
 //           exchanged through distributed shared memory).
 //   pass 2  a key is admitted when its tensor-core score reaches
-//           (bound - margin); about 75 keys per row and CTA at K = 128.  Admitted
-//           keys are queued per warp and rescored exactly in fp32 by all 32
-//           lanes together (sequential FMA over d from the q tile and the staged
-//           key rows: the arithmetic of the CUDA-core kernel).
-//   output  rescored candidates go straight to a caller-provided workspace, one
-//           list of KW slots per (row, CTA, warp) with the count in a register
-//           (KW = 256 for K <= 128, 384 for K <= 256); a list within 64 of full
-//           is compacted to its exact top-K (warp radix select), which raises the
-//           row's admission threshold.  topk_finalize_kernel, launched right after
-//           at full occupancy (one warp per row), selects the exact top-K of the
-//           four lists and writes the indices and pads.  Batches larger
+//           (bound - margin); about 75 keys per row and CTA at K = 128.  The
+//           lane that owns the row appends the key's index to its own list in a
+//           caller-provided workspace, one list of KW slots per (row, CTA, warp)
+//           with the count in a register (KW = 256 for K <= 128, 384 for
+//           K <= 256).  A list within 64 of full is compacted to its exact top-K
+//           (its entries rescored exactly from the address rows in global
+//           memory, then a warp radix select), which raises the row's admission
+//           threshold.  Nothing else is rescored here: that work would sit on
+//           this kernel's critical chain of chunks.
+//   output  topk_rescore_kernel (one warp per list, full occupancy) computes the
+//           exact fp32 score of every candidate of rows holding more than K
+//           (sequential FMA over d: the CUDA-core kernel's arithmetic), and
+//           topk_finalize_kernel (one warp per row) selects the exact top-K of
+//           the four lists and writes the indices and pads.  Batches larger
 //           than about 65536 query rows run in slices that reuse the workspace.
+// The selection warps also take max|k| over the chunks they score (for the
+// margin), so the producer warp only loads and issues MMAs.
 // The margin, 2^-13 * sum_d |q_d| * max|k|, exceeds any plausible accumulation
 // error of a 32-term fp32 dot product with exact bf16/fp16 products, so every
 // key whose exact score reaches the K-th best is admitted: the result is exact
@@ -63,7 +68,6 @@ constexpr int kN = 128;   // keys per chunk = MMA N
 constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant
 constexpr int kThreads = (kEpiWarps + 1) * 32;
 constexpr int kGroups = 256;  // pass-1 key groups per row (TMEM columns 256..511)
-constexpr int kQcap = 2048;   // rescoring queue entries per warp (one chunk admits at most 64 x 32)
 // Workspace list capacity KW per (row, CTA, warp) is a template parameter: 256 for
 // K <= 128 and 384 for K <= 256 (a list within 64 of full is compacted to its top-K,
 // which leaves room for the next chunk).
@@ -75,6 +79,14 @@ constexpr float kEpsScale = 1.0f / 8192.0f;
 constexpr int kMaxDevices = 64;
 constexpr size_t kMaxSmem = 232448;
 
+// Address rows in their input type (fp32 addresses: the original fp32 rows, not
+// the bf16 copies the tensor cores read), element strides.
+struct ScoreSrc {
+  const void* q;
+  const void* k;
+  int64_t qsb, qst, ksb, kst;
+};
+
 struct TcParams {
   const void* q;
   int64_t qsb, qst;
@@ -83,7 +95,7 @@ struct TcParams {
   int rt, rs, r0;
   int32_t* idx;
   int32_t* status;
-  uint64_t* ws;      // [B*Tq][kLists][KW] candidate composites (key << 32 | ~index)
+  int32_t* ws;       // [B*Tq][kLists][KW] candidate key indices
   int32_t* ws_cnt;   // [B*Tq][kLists] candidate counts
   const int32_t* lim;  // optional [B][Tq] per-row key limits (see TopkParams)
   // Test hook, set by wf_testing_withhold_pair_arrive (0 = off): CTA 1 of every pair
@@ -95,6 +107,7 @@ struct TcParams {
   const float* qf;
   const float* kf;
   int64_t fqsb, fqst, fksb, fkst;
+  ScoreSrc src;  // address rows for exact rescoring
 };
 
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -117,8 +130,7 @@ struct Layout {
   static constexpr size_t off_misc = off_bar + 8 * n_bar;  // tmem base, kmax own, kmax peer, abort
   static constexpr size_t off_xslot = align_up(off_misc + 16, 16);  // [2 parities][kM rows][4] bisection exchange
   static constexpr size_t off_xpair = off_xslot + 4 * 2 * kM * 4;  // [2 parities][2 warps][kM][4] pair sums
-  static constexpr size_t off_queue = off_xpair + 4 * 2 * 2 * kM * 4;
-  static constexpr size_t off_merge = off_queue + 4 * (size_t)kQcap * kEpiWarps;  // per warp: KB keys + KB indices
+  static constexpr size_t off_merge = off_xpair + 4 * 2 * 2 * kM * 4;  // per warp: KB keys + KB indices
   static constexpr size_t bytes = off_merge + (size_t)kEpiWarps * KB * (4 + 4);
   // Slack to align the dynamic base to 1024, and at least 116 KB in total: two of
   // these CTAs must never share an SM (each allocates all 512 TMEM columns), while
@@ -133,6 +145,10 @@ struct Layout {
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, kWaitLimitNs));
 }
+// Named barrier of all selection warps.
+__device__ __forceinline__ void sel_sync() {
+  asm volatile("bar.sync 5, %0;" ::"n"(kEpiWarps * 32) : "memory");
+}
 // Named barrier of the 64 threads of one quadrant's two warps.
 __device__ __forceinline__ void pair_sync(int id) {
   asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
@@ -142,18 +158,16 @@ __device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity
   return __all_sync(0xffffffffu, mbar_wait_cluster(bar, parity, limit_ns));
 }
 
-template <typename TI, int ROWB>
-__device__ __forceinline__ float dot_swizzled(const unsigned char* qtile, int qr, const unsigned char* stage, int kr) {
-  const int swq = (qr * ROWB >> 7) & (ROWB / 16 - 1);
-  const int swk = (kr * ROWB >> 7) & (ROWB / 16 - 1);
-  const unsigned char* qrow = qtile + qr * ROWB;
-  const unsigned char* krow = stage + kr * ROWB;
+// Exact fp32 score of two bf16 / fp16 rows: sequential FMA over d in order, with
+// both operands converted to fp32 (the CUDA-core kernel's arithmetic).
+template <typename TI, int R>
+__device__ __forceinline__ float dot_rows(const TI* qrow, const TI* krow) {
   float acc = 0.f;
 #pragma unroll
-  for (int c = 0; c < ROWB / 16; ++c) {
+  for (int c = 0; c < R / 8; ++c) {
     float a[8], b[8];
-    Vec16<TI>::unpack(*reinterpret_cast<const uint4*>(qrow + ((c ^ swq) << 4)), a);
-    Vec16<TI>::unpack(*reinterpret_cast<const uint4*>(krow + ((c ^ swk) << 4)), b);
+    Vec16<TI>::unpack(ldg16(qrow + c * 8), a);
+    Vec16<TI>::unpack(ldg16(krow + c * 8), b);
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc = fmaf(a[e], b[e], acc);
   }
@@ -175,6 +189,17 @@ __device__ __forceinline__ float dot_f32_rows(const float* qrow, const float* kr
     acc = fmaf(a.w, b.w, acc);
   }
   return acc;
+}
+
+// Exact fp32 score of query row `qrow` and key `key` of batch element b.
+template <typename TI, int R, bool F32>
+__device__ __forceinline__ float exact_score(const ScoreSrc& s, int b, int qrow, int key) {
+  if constexpr (F32)
+    return dot_f32_rows<R>(static_cast<const float*>(s.q) + (int64_t)b * s.qsb + (int64_t)qrow * s.qst,
+                           static_cast<const float*>(s.k) + (int64_t)b * s.ksb + (int64_t)key * s.kst);
+  else
+    return dot_rows<TI, R>(static_cast<const TI*>(s.q) + (int64_t)b * s.qsb + (int64_t)qrow * s.qst,
+                           static_cast<const TI*>(s.k) + (int64_t)b * s.ksb + (int64_t)key * s.kst);
 }
 
 // F32: fp32 addresses.  The tensor cores score bf16 copies (TI = bf16); every
@@ -212,7 +237,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(base + L::off_misc);
   uint32_t* kmax_own_s = tmem_base_s + 1;
   uint32_t* kmax_in_s = tmem_base_s + 2;
-  uint32_t* queues = reinterpret_cast<uint32_t*>(base + L::off_queue);
   uint32_t* xslot = reinterpret_cast<uint32_t*>(base + L::off_xslot);
   uint32_t* xpair = reinterpret_cast<uint32_t*>(base + L::off_xpair);
   uint32_t* mkey = reinterpret_cast<uint32_t*>(base + L::off_merge);       // [warp][KB]
@@ -240,8 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&done[s], kEpiWarps);
     }
     mbar_init(qbar, 1);
-    for (int i = 0; i < kXRounds; ++i) mbar_init(&xbar[i], 2 * kM);  // both warps of a quadrant post a row
-    mbar_init(kbar, 2 * kM);
+    for (int i = 0; i < kXRounds; ++i) mbar_init(&xbar[i], kM);  // the quadrant's first warp posts a row
+    mbar_init(kbar, kM);
     mbar_init(drain, 1);
     *kmax_own_s = 0u;
     fence_mbarrier_init();
@@ -278,7 +302,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     ok = warp_wait(qbar, 0);
     const bool q_landed = ok;
     if (!ok) why |= 4;
-    uint32_t kbits = 0;
     for (int w = 0; w < n_work && ok; ++w) {
       const int s = w % S;
       unsigned char* stage = ks + s * L::STAGE_STRIDE;
@@ -296,23 +319,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_f16(d, a, bd, IDESC, kk > 0);
         }
         mma_commit(&mdone[s]);
-      }
-      if (w < n_own) {
-        // max |k| over the chunk (bit patterns of non-negative floats order like values)
-        const uint4* v = reinterpret_cast<const uint4*>(stage);
-        uint32_t m2 = 0;
-        for (int i = lane; i < (int)(L::STAGE_BYTES / 16); i += 32) {
-          const uint4 x = v[i];
-          m2 = __vmaxu2(m2, x.x & 0x7fff7fffu);
-          m2 = __vmaxu2(m2, x.y & 0x7fff7fffu);
-          m2 = __vmaxu2(m2, x.z & 0x7fff7fffu);
-          m2 = __vmaxu2(m2, x.w & 0x7fff7fffu);
-        }
-        kbits = max(kbits, __reduce_max_sync(kFullMask, max(m2 & 0xffffu, m2 >> 16)));
-        if (w == n_own - 1 && lane == 0) {
-          const float km = kBf16 ? __uint_as_float(kbits << 16) : __half2float(__ushort_as_half((unsigned short)kbits));
-          *kmax_own_s = __float_as_uint(km);
-        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&mdone[s]);
@@ -382,10 +388,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok) why |= 64;
 
     // ---------------- pass 1: group maxima of tensor-core scores (this warp's slices)
+    // The selection warps also take max|k| over the CTA's chunks (bit patterns of
+    // non-negative floats order like their values), each warp over 1/8 of a stage.
+    uint32_t kbits = 0;
     for (int w = 0; w < n_own && ok; ++w) {
       const int s = w % S;
-      if (!warp_wait(&mdone[s], (uint32_t)(w / S) & 1u)) { ok = false; why |= 128; break; }
+      const uint32_t ph = (uint32_t)(w / S) & 1u;
+      if (!warp_wait(&mdone[s], ph) || !warp_wait(&full[s], ph)) { ok = false; why |= 128; break; }
       tc_fence_after();
+      {
+        const uint4* kv = reinterpret_cast<const uint4*>(ks + s * L::STAGE_STRIDE);
+        uint32_t m2 = 0;
+        for (int i = warp * 32 + lane; i < (int)(L::STAGE_BYTES / 16); i += kEpiWarps * 32) {
+          const uint4 x = kv[i];
+          m2 = __vmaxu2(m2, x.x & 0x7fff7fffu);
+          m2 = __vmaxu2(m2, x.y & 0x7fff7fffu);
+          m2 = __vmaxu2(m2, x.z & 0x7fff7fffu);
+          m2 = __vmaxu2(m2, x.w & 0x7fff7fffu);
+        }
+        kbits = max(kbits, max(m2 & 0xffffu, m2 >> 16));
+      }
       const int c = chunk_of(w);
       const uint32_t acc = tmem_base + lane_base + (uint32_t)((w & 1) * kN);
       const uint32_t gcol = tmem_base + lane_base + 256 + (uint32_t)((w & 1) * kN);
@@ -423,6 +445,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // both warps' group maxima are complete and visible to the pair
     tmem_st_wait();
+    kbits = __reduce_max_sync(kFullMask, kbits);
+    if (lane == 0) atomicMax(kmax_own_s, kbits);
     tc_fence_before();
     pair_sync(pair_bar);
     tc_fence_after();
@@ -467,15 +491,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       x[1] = __float_as_uint(fminf(__uint_as_float(x[1]), __uint_as_float(other[1])));
       x[2] = __float_as_uint(fmaxf(__uint_as_float(x[2]), __uint_as_float(other[2])));
     };
-    // one exchange with the peer CTA: send (a, b, c) to the peer's thread of this row
-    // (both warps of the quadrant send the same triple), receive the peer's triple
+    // one exchange with the peer CTA: the quadrant's first warp sends (a, b, c) to the
+    // peer's thread of this row (both warps hold the same triple); both warps wait
+    // for and read the peer's triple
     auto swap3 = [&](int round, const uint32_t (&x)[3], uint32_t (&got)[3]) {
       uint32_t* slot = xslot + ((round & 1) * kM + r) * 4;
-      const uint32_t peer_slot = map_peer(slot, peer);
-      st_peer_u32(peer_slot, x[0]);
-      st_peer_u32(peer_slot + 4, x[1]);
-      st_peer_u32(peer_slot + 8, x[2]);
-      if (!(p.withhold == round + 1 && rank == 1)) mbar_arrive_peer(map_peer(&xbar[round], peer));
+      if (hf == 0) {
+        const uint32_t peer_slot = map_peer(slot, peer);
+        st_peer_u32(peer_slot, x[0]);
+        st_peer_u32(peer_slot + 4, x[1]);
+        st_peer_u32(peer_slot + 8, x[2]);
+        if (!(p.withhold == round + 1 && rank == 1)) mbar_arrive_peer(map_peer(&xbar[round], peer));
+      }
       if (!warp_wait_cluster(&xbar[round], 0, p.xwait_ns)) { ok = false; why |= 256; }
       got[0] = slot[0];
       got[1] = slot[1];
@@ -514,61 +541,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const float theta = bis ? lo : -INFINITY;
 
-    // key magnitudes for the margin: the peer's arrives with the first exchange
-    if (r == 0 && hf == 0) st_peer_u32(map_peer(kmax_in_s, peer), *kmax_own_s);
-    mbar_arrive_peer(map_peer(kbar, peer));
+    // key magnitudes for the margin (16-bit patterns; the barrier spans every
+    // selection warp, so all their parts are in)
+    sel_sync();
+    if (hf == 0) {
+      if (r == 0) st_peer_u32(map_peer(kmax_in_s, peer), *kmax_own_s);
+      mbar_arrive_peer(map_peer(kbar, peer));
+    }
     if (!warp_wait_cluster(kbar, 0)) { ok = false; why |= 1024; }
-    const float kpair = fmaxf(__uint_as_float(*kmax_own_s), __uint_as_float(*kmax_in_s));
+    const uint32_t kb = max(*kmax_own_s, *kmax_in_s);
+    const float kpair = kBf16 ? __uint_as_float(kb << 16) : __half2float(__ushort_as_half((unsigned short)kb));
     const float eps = (F32 ? 1.0f / 64.0f : kEpsScale) * qabs * kpair;
     float lim = theta > -INFINITY ? theta - eps : -INFINITY;
 
-    // ---------------- pass 2: admit, rescore exactly, keep candidates in the workspace
-    uint32_t* queue = queues + warp * kQcap;
+    // ---------------- pass 2: admit candidates into the workspace lists
+    // A key is admitted when its tensor-core score reaches lim.  Only its index is
+    // stored; the exact fp32 scores are computed by the finalisation kernel, which
+    // runs at full occupancy, so this kernel's critical chain holds no rescoring.
     const int64_t row0 = (int64_t)b * p.Tq + l0 + 32 * qd;  // first row of this quadrant
-    int qsize = 0;  // warp-uniform
 
     // This warp's candidates of row r go to its own list (CTA rank, column half hf):
     // the count lives in the lane's register, so no slot is shared with another warp.
     int cnt = 0;
-
-    auto flush = [&](const unsigned char* stage, int c) {
-      __syncwarp();
-      for (int e = lane; e < qsize; e += 32) {
-        const uint32_t ent = queue[e];
-        const int lr = ent & 31, jj = (ent >> 5) & 127, dest = (int)(ent >> 12);
-        float ex;
-        if constexpr (F32)
-          ex = dot_f32_rows<R>(p.qf + (int64_t)b * p.fqsb + (int64_t)(l0 + 32 * qd + lr) * p.fqst,
-                               p.kf + (int64_t)b * p.fksb + (int64_t)(c * kN + jj) * p.fkst);
-        else
-          ex = dot_swizzled<TI, ROWB>(qs, 32 * qd + lr, stage, jj);
-        p.ws[(((row0 + lr) * 2 + rank) * 2 + hf) * KW + dest] =
-            ((uint64_t)ordered_key(ex) << 32) | (uint32_t)(~(uint32_t)(c * kN + jj));
-      }
-      __syncwarp();
-      qsize = 0;
-    };
+    int32_t* mylist = p.ws + (((row0 + lane) * 2 + rank) * 2 + hf) * KW;
 
     bool alive = ok;
     for (int w = n_own; w < n_work; ++w) {
       const int s = w % S;
       const uint32_t ph = (uint32_t)(w / S) & 1u;
-      if (alive && (!warp_wait(&mdone[s], ph) || !warp_wait(&full[s], ph))) {
+      if (alive && !warp_wait(&mdone[s], ph)) {
         alive = false;
         ok = false;
         why |= 512;
       }
       tc_fence_after();
       const int c = chunk_of(w);
-      const unsigned char* stage = ks + s * L::STAGE_STRIDE;
       const uint32_t acc = tmem_base + lane_base + (uint32_t)((w & 1) * kN);
       // admission masks of both slices (loads in flight together)
-      uint32_t masks[2] = {0u, 0u};
+      uint32_t v[2][32];
       if (alive) {
-        uint32_t v[2][32];
         tmem_ld_32x32b_x32(acc + (2 * hf) * 32, v[0]);
         tmem_ld_32x32b_x32(acc + (2 * hf + 1) * 32, v[1]);
         tmem_ld_wait();
+      }
+      // the scores are in registers: the accumulator and the stage are free
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&done[s]);
+      uint32_t masks[2] = {0u, 0u};
+      if (alive) {
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           uint32_t m = 0;
@@ -582,62 +603,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int np = __popc(masks[0]) + __popc(masks[1]);
       // A list that this chunk could overflow is compacted to its exact top-K first
-      // (queued entries written out beforehand); that also raises the row's threshold.
+      // (its entries rescored exactly from the address rows in global memory); that
+      // also raises the row's threshold.  Rare: a row admits ~1.2 K keys in all.
       unsigned need = __ballot_sync(kFullMask, cnt + np > KW);
-      if (need) {
-        flush(stage, c);
+      while (need) {
+        const int ln = __ffs(need) - 1;
+        need &= need - 1;
+        const int n = __shfl_sync(kFullMask, cnt, ln);
+        int32_t* wrow = p.ws + (((row0 + ln) * 2 + rank) * 2 + hf) * KW;
+        const int qrow = l0 + 32 * qd + ln;
+        uint32_t kk[KW / 32];
+        int ii[KW / 32];
+#pragma unroll
+        for (int t = 0; t < KW / 32; ++t) {
+          const int e = t * 32 + lane;
+          const int j = e < n ? wrow[e] : 0;
+          kk[t] = e < n ? ordered_key(exact_score<TI, R, F32>(p.src, b, qrow, j)) : 0u;
+          ii[t] = e < n ? j : INT_MAX;
+        }
         uint32_t* bk = mkey + warp * KB;
         int* bi = midx + warp * KB;
-        while (need) {
-          const int ln = __ffs(need) - 1;
-          need &= need - 1;
-          const int n = __shfl_sync(kFullMask, cnt, ln);
-          uint64_t* wrow = p.ws + (((row0 + ln) * 2 + rank) * 2 + hf) * KW;
-          uint32_t kk[KW / 32];
-          int ii[KW / 32];
-#pragma unroll
-          for (int t = 0; t < KW / 32; ++t) {
-            const int e = t * 32 + lane;
-            const uint64_t cv = e < n ? wrow[e] : 0ull;
-            kk[t] = (uint32_t)(cv >> 32);
-            ii[t] = e < n ? (int)(~(uint32_t)cv) : INT_MAX;
-          }
-          const uint32_t tau = select_compact<KW / 32>(kk, ii, n, p.K, lane, bk, bi);
-          for (int e = lane; e < p.K; e += 32) wrow[e] = ((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e]);
-          __syncwarp();
-          if (lane == ln) {
-            cnt = p.K;
-            lim = fmaxf(lim, key_to_float(tau) - eps);
-          }
+        const uint32_t tau = select_compact<KW / 32>(kk, ii, n, p.K, lane, bk, bi);
+        for (int e = lane; e < p.K; e += 32) wrow[e] = bi[e];
+        __syncwarp();
+        if (lane == ln) {
+          cnt = p.K;
+          lim = fmaxf(lim, key_to_float(tau) - eps);
         }
       }
-      // slots of this lane's admitted keys: its own list, no other writer
-      const int base = cnt;
-      cnt += np;
-      int incl = np;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(kFullMask, incl, o);
-        if (lane >= o) incl += t;
-      }
-      const int total = __shfl_sync(kFullMask, incl, 31);
-      if (qsize + total > kQcap) flush(stage, c);
-      uint32_t* qp = queue + qsize + incl - np;
-      uint32_t slot = (uint32_t)base;
+      // this lane's admitted keys go to its own list
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         uint32_t m = masks[i];
         while (m) {
           const int j = __ffs(m) - 1;
           m &= m - 1;
-          *qp++ = (uint32_t)lane | ((uint32_t)((2 * hf + i) * 32 + j) << 5) | (slot++ << 12);
+          mylist[cnt++] = c * kN + (2 * hf + i) * 32 + j;
         }
       }
-      qsize += total;
-      flush(stage, c);  // the stage is about to be released
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&done[s]);
     }
     if (row_ok) p.ws_cnt[((row0 + lane) * 2 + rank) * 2 + hf] = cnt;
   }
@@ -657,13 +660,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 // index), in list order, plus pad slots.  Runs at full occupancy; the
 // selection is the same warp radix select the streaming kernels use.
 struct FinParams {
-  const uint64_t* ws;
+  const int32_t* ws;
+  uint32_t* ws_key;  // exact keys of the candidates, written by topk_rescore_kernel
   const int32_t* ws_cnt;
   int32_t* idx;
   int B, Tq, Tk, K, cap;
   int pad_mode;
   int rt, rs, r0;
   const int32_t* lim;
+  ScoreSrc src;
 };
 
 constexpr int kFinWarps = 8;
@@ -674,7 +679,8 @@ __device__ __forceinline__ void finalize_row(const FinParams& p, int64_t row, co
   const int l = (int)(row % p.Tq);
   const int g = p.lim ? p.lim[row] - 1 : ((l / p.rt) * p.rs + p.r0) * p.rt + (l % p.rt);
   const int e1 = nl[0], e2 = e1 + nl[1], e3 = e2 + nl[2], n = e3 + nl[3];
-  const uint64_t* a = p.ws + row * kLists * p.cap;
+  const int32_t* a = p.ws + row * kLists * p.cap;
+  const uint32_t* ak = p.ws_key + row * kLists * p.cap;
   // The row's concatenated lists are consumed in blocks of up to 32*EPLF entries
   // together with the running top-K kept in bk/bi (one block in the usual case).
   int m = 0;   // entries held in bk/bi
@@ -687,17 +693,20 @@ __device__ __forceinline__ void finalize_row(const FinParams& p, int64_t row, co
 #pragma unroll
     for (int t = 0; t < EPLF; ++t) {
       const int e = t * 32 + lane;
-      uint64_t c = 0;
+      uint32_t key = 0;
+      int j = INT_MAX;
       if (e < m) {
-        c = ((uint64_t)bk[e] << 32) | (uint32_t)(~(uint32_t)bi[e]);
+        key = bk[e];
+        j = bi[e];
       } else if (e < cnt) {
         const int x = e0 + e - m;
         const int li = (x >= e1) + (x >= e2) + (x >= e3);
         const int off = li == 0 ? 0 : li == 1 ? e1 : li == 2 ? e2 : e3;
-        c = a[li * p.cap + (x - off)];
+        j = a[li * p.cap + (x - off)];
+        key = ak[li * p.cap + (x - off)];
       }
-      kk[t] = (uint32_t)(c >> 32);
-      ii[t] = e < cnt ? (int)(~(uint32_t)c) : INT_MAX;
+      kk[t] = key;
+      ii[t] = j;
     }
     __syncwarp();
     if (cnt > p.K) {
@@ -750,6 +759,58 @@ __global__ void __launch_bounds__(kFinWarps * 32, 2) topk_finalize_kernel(const 
   constexpr int E1 = KB <= 128 ? 6 : 12, E2 = KB <= 128 ? 12 : 16;
   if (n <= E1 * 32) finalize_row<E1, SE>(p, row, nl, lane, skey[warp], sidx[warp]);
   else finalize_row<E2, SE>(p, row, nl, lane, skey[warp], sidx[warp]);
+}
+
+// Exact fp32 keys of every candidate: one warp per (row, list), full occupancy.
+// Rows whose lists hold K candidates or fewer need no selection and are skipped.
+template <typename TI, int R, bool F32>
+__global__ void __launch_bounds__(256) topk_rescore_kernel(const FinParams p) {
+  const int64_t wl = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);  // (row, list)
+  const int lane = threadIdx.x & 31;
+  if (wl >= (int64_t)p.B * p.Tq * kLists) return;
+  const int64_t row = wl / kLists;
+  const int4 c4 = *reinterpret_cast<const int4*>(p.ws_cnt + row * kLists);
+  if (c4.x + c4.y + c4.z + c4.w <= p.K) return;
+  const int n = p.ws_cnt[wl];
+  const int l = (int)(row % p.Tq), bb = (int)(row / p.Tq);
+  const int32_t* a = p.ws + wl * p.cap;
+  uint32_t* ak = p.ws_key + wl * p.cap;
+  // two entries per lane in flight: both indices, then both key rows, then the FMAs
+  for (int e0 = 0; e0 < n; e0 += 64) {
+    const int e1 = e0 + lane, e2 = e1 + 32;
+    const int j1 = e1 < n ? a[e1] : -1;
+    const int j2 = e2 < n ? a[e2] : -1;
+    if constexpr (F32 || R > 32) {
+      if (j1 >= 0) ak[e1] = ordered_key(exact_score<TI, R, F32>(p.src, bb, l, j1));
+      if (j2 >= 0) ak[e2] = ordered_key(exact_score<TI, R, F32>(p.src, bb, l, j2));
+    } else {
+      constexpr int NC = R / 8;
+      const TI* qrow = static_cast<const TI*>(p.src.q) + (int64_t)bb * p.src.qsb + (int64_t)l * p.src.qst;
+      const TI* kb = static_cast<const TI*>(p.src.k) + (int64_t)bb * p.src.ksb;
+      uint4 qv[NC], k1[NC], k2[NC];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        qv[c] = ldg16(qrow + c * 8);
+        k1[c] = j1 >= 0 ? ldg16(kb + (int64_t)j1 * p.src.kst + c * 8) : make_uint4(0, 0, 0, 0);
+        k2[c] = j2 >= 0 ? ldg16(kb + (int64_t)j2 * p.src.kst + c * 8) : make_uint4(0, 0, 0, 0);
+      }
+      float d1 = 0.f, d2 = 0.f;
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        float x[8], y1[8], y2[8];
+        Vec16<TI>::unpack(qv[c], x);
+        Vec16<TI>::unpack(k1[c], y1);
+        Vec16<TI>::unpack(k2[c], y2);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          d1 = fmaf(x[t], y1[t], d1);
+          d2 = fmaf(x[t], y2[t], d2);
+        }
+      }
+      if (j1 >= 0) ak[e1] = ordered_key(d1);
+      if (j2 >= 0) ak[e2] = ordered_key(d2);
+    }
+  }
 }
 
 // ---------------------------------------------------------------- host side
@@ -814,7 +875,8 @@ int64_t batch_per_pass(int64_t B, int64_t Tq) {
   return bpp < B ? bpp : B;
 }
 
-size_t ws_bytes_per_row(int K) { return (size_t)kLists * list_capacity(K) * sizeof(uint64_t) + kLists * sizeof(int32_t); }
+// per row: kLists lists of candidate indices and their exact keys, and the list counts
+size_t ws_bytes_per_row(int K) { return (size_t)kLists * list_capacity(K) * 2 * sizeof(int32_t) + kLists * sizeof(int32_t); }
 
 // bf16 copies of fp32 address rows (F32 path): dst[b][t][r] contiguous.
 __global__ void shadow_bf16_kernel(const float* src, int64_t sb, int64_t st, int nb, int T, int R,
@@ -852,8 +914,9 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
   const size_t lists = rows_pass * ws_bytes_per_row(p.K);
   const size_t need = lists + (F32 ? shadow_bytes_pass(bpp, p.Tq, p.Tk, R) : 0);
   if (!p.ws || p.ws_bytes < need || reinterpret_cast<uintptr_t>(p.ws) % 16) return -3;
-  uint64_t* ws = reinterpret_cast<uint64_t*>(p.ws);
-  int32_t* ws_cnt = reinterpret_cast<int32_t*>(ws + rows_pass * kLists * KW);
+  int32_t* ws = reinterpret_cast<int32_t*>(p.ws);
+  uint32_t* ws_key = reinterpret_cast<uint32_t*>(ws + rows_pass * kLists * KW);
+  int32_t* ws_cnt = reinterpret_cast<int32_t*>(ws_key + rows_pass * kLists * KW);
   __nv_bfloat16* shq = reinterpret_cast<__nv_bfloat16*>(
       (reinterpret_cast<uintptr_t>(static_cast<char*>(p.ws) + lists) + 255) & ~uintptr_t(255));
   __nv_bfloat16* shk = shq + (size_t)bpp * p.Tq * R;
@@ -893,6 +956,7 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
     t.status = p.status;
     t.ws = ws;
     t.ws_cnt = ws_cnt;
+    t.src = ScoreSrc{q, k, p.qsb, p.qst, p.ksb, p.kst};
     t.withhold = g_test_withhold.exchange(0);
     t.xwait_ns = t.withhold ? g_test_xwait_ns.load() : kWaitLimitNs;
 
@@ -913,12 +977,15 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
     FinParams f{};
     f.ws = ws;
     f.ws_cnt = ws_cnt;
+    f.ws_key = ws_key;
     f.idx = t.idx;
     f.B = nb; f.Tq = p.Tq; f.Tk = p.Tk; f.K = p.K; f.cap = KW;
     f.pad_mode = p.pad_mode;
     f.rt = p.rt; f.rs = p.rs; f.r0 = p.r0;
     f.lim = t.lim;
+    f.src = t.src;
     const size_t rows = (size_t)nb * p.Tq;
+    topk_rescore_kernel<TI, R, F32><<<(unsigned)((rows * kLists + 7) / 8), 256, 0, stream>>>(f);
     topk_finalize_kernel<SE, KW - 128><<<(unsigned)((rows + kFinWarps - 1) / kFinWarps), kFinWarps * 32, 0, stream>>>(f);
     e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
