@@ -366,7 +366,7 @@ WF_API int wf_gather_rows_bulk_bench(const void* k, const void* v, int64_t row_s
 /*
  * Test hook, no counterpart in the reference: makes the next tensor-core retrieval
  * launch on this process exercise its timeout path without any fault.  CTA 1 of
- * every CTA pair skips its arrive on the peer's barrier of bisection exchange
+ * every CTA pair skips its send to the peer CTA in bisection exchange
  * `round` (0..7; negative turns the hook off), and the exchange waits give up after
  * wait_limit_ns.  The waiting CTA then sets status bits 1 and 8 (wait site 256),
  * drains its own copies and MMAs, frees its tensor memory and returns; the output

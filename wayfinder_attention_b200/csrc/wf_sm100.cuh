@@ -184,6 +184,21 @@ __device__ __forceinline__ uint32_t map_peer(const void* p, uint32_t rank) {
 __device__ __forceinline__ void st_peer_u32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
+// Asynchronous remote stores into a peer CTA's shared memory: each completes its
+// bytes on the peer's mbarrier (whose owner posted expect_tx), so the receiver
+// needs no per-sender arrive and the sender no cluster-scope fence.
+__device__ __forceinline__ void st_async_v4(uint32_t peer_addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d,
+                                            uint32_t peer_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   peer_addr),
+               "r"(a), "r"(b), "r"(c), "r"(d), "r"(peer_bar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_u32(uint32_t peer_addr, uint32_t v, uint32_t peer_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(peer_addr), "r"(v),
+               "r"(peer_bar)
+               : "memory");
+}
 __device__ __forceinline__ uint32_t ld_peer_u32(uint32_t addr) {
   uint32_t v;
   asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");

@@ -23,7 +23,8 @@
 //           chunk in the CTA's stream).  The K-th largest of the pair's 512 group
 //           maxima is the score of K distinct keys, so it lower-bounds the row's
 //           K-th best score; the two CTAs bisect it together (7 steps, counts
-//           exchanged through distributed shared memory).
+//           exchanged through distributed shared memory with asynchronous
+//           stores that complete on the receiver's barrier).
 //   pass 2  a key is admitted when its tensor-core score reaches
 //           (bound - margin); about 75 keys per row and CTA at K = 128.  The
 //           lane that owns the row appends the key's index to its own list in a
@@ -99,7 +100,7 @@ struct TcParams {
   int32_t* ws_cnt;   // [B*Tq][kLists] candidate counts
   const int32_t* lim;  // optional [B][Tq] per-row key limits (see TopkParams)
   // Test hook, set by wf_testing_withhold_pair_arrive (0 = off): CTA 1 of every pair
-  // skips its arrive on the peer's barrier of bisection exchange (withhold - 1), and
+  // skips its send to the peer in bisection exchange (withhold - 1), and
   // the waits of the exchanges give up after xwait_ns, so CTA 0's wait runs out.
   int withhold;
   uint64_t xwait_ns;
@@ -264,8 +265,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&done[s], kEpiWarps);
     }
     mbar_init(qbar, 1);
-    for (int i = 0; i < kXRounds; ++i) mbar_init(&xbar[i], kM);  // the quadrant's first warp posts a row
-    mbar_init(kbar, kM);
+    // exchange barriers complete on bytes: one local expect_tx arrive each, and the
+    // peer's asynchronous stores (16 bytes per row per round; 4 bytes of key magnitude)
+    for (int i = 0; i < kXRounds; ++i) mbar_init(&xbar[i], 1);
+    mbar_init(kbar, 1);
     mbar_init(drain, 1);
     *kmax_own_s = 0u;
     fence_mbarrier_init();
@@ -492,17 +495,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       x[2] = __float_as_uint(fmaxf(__uint_as_float(x[2]), __uint_as_float(other[2])));
     };
     // one exchange with the peer CTA: the quadrant's first warp sends (a, b, c) to the
-    // peer's thread of this row (both warps hold the same triple); both warps wait
-    // for and read the peer's triple
+    // peer's thread of this row with one asynchronous 16-byte store that completes on
+    // the peer's barrier of this round (both warps hold the same triple); both warps
+    // wait for and read the peer's triple
     auto swap3 = [&](int round, const uint32_t (&x)[3], uint32_t (&got)[3]) {
       uint32_t* slot = xslot + ((round & 1) * kM + r) * 4;
-      if (hf == 0) {
-        const uint32_t peer_slot = map_peer(slot, peer);
-        st_peer_u32(peer_slot, x[0]);
-        st_peer_u32(peer_slot + 4, x[1]);
-        st_peer_u32(peer_slot + 8, x[2]);
-        if (!(p.withhold == round + 1 && rank == 1)) mbar_arrive_peer(map_peer(&xbar[round], peer));
-      }
+      if (warp == 0 && lane == 0) mbar_arrive_expect_tx(&xbar[round], (uint32_t)(kM * 16));
+      if (hf == 0 && !(p.withhold == round + 1 && rank == 1))
+        st_async_v4(map_peer(slot, peer), x[0], x[1], x[2], 0u, map_peer(&xbar[round], peer));
       if (!warp_wait_cluster(&xbar[round], 0, p.xwait_ns)) { ok = false; why |= 256; }
       got[0] = slot[0];
       got[1] = slot[1];
@@ -544,9 +544,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // key magnitudes for the margin (16-bit patterns; the barrier spans every
     // selection warp, so all their parts are in)
     sel_sync();
-    if (hf == 0) {
-      if (r == 0) st_peer_u32(map_peer(kmax_in_s, peer), *kmax_own_s);
-      mbar_arrive_peer(map_peer(kbar, peer));
+    if (r == 0 && hf == 0) {
+      mbar_arrive_expect_tx(kbar, 4u);
+      st_async_u32(map_peer(kmax_in_s, peer), *kmax_own_s, map_peer(kbar, peer));
     }
     if (!warp_wait_cluster(kbar, 0)) { ok = false; why |= 1024; }
     const uint32_t kb = max(*kmax_own_s, *kmax_in_s);
