@@ -128,7 +128,9 @@ class ClockSampler:
             pynvml.nvmlInit()
             self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
-            time.sleep(0.005)  # first sample before the timed region starts
+            t0 = time.time()  # the first sample lands before the timed region starts
+            while not self.samples and self._thread.is_alive() and time.time() - t0 < 2.0:
+                time.sleep(0.001)
         except Exception:
             self._thread = None
         return self
