@@ -75,6 +75,7 @@ __device__ __forceinline__ int64_t kv_row_offset(const AttnParams& p, int j, int
 // instantiation keeps the address arithmetic of the plain layout minimal.
 template <typename TI, typename TO, int D, int E, bool CYC, bool DROP>
 __global__ void __launch_bounds__(256) sparse_attn_kernel(const AttnParams p, int warps_per_block) {
+  pdl_wait();
   using V16 = Vec16<TI>;
   constexpr int VEC = V16::N;
   constexpr int NV = E / VEC;       // 16-byte vectors per lane and row
@@ -292,8 +293,8 @@ int launch_t(const AttnParams& p, cudaStream_t stream) {
   }
   const int64_t work = (int64_t)p.B * p.Tq * ngroups;
   const int64_t blocks = (work + wpb - 1) / wpb;
-  kern<<<(unsigned)blocks, wpb * 32, smem, stream>>>(p, wpb);
-  return (int)cudaGetLastError();
+  const cudaError_t e = launch_pdl(kern, dim3((unsigned)blocks), dim3(wpb * 32), smem, stream, p, wpb);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 // E: elements per lane.  16 when the heads of a query span at least 512

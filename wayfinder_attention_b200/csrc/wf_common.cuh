@@ -4,6 +4,7 @@
 // selector, and warp reductions.  Everything here is plain CUDA C++; the
 // tensor-core scoring path adds its own PTX wrappers in wf_tc.cuh.
 #pragma once
+#include <utility>
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -11,6 +12,29 @@
 #include <stdint.h>
 
 namespace wf {
+
+// Programmatic dependent launch: a kernel launched with launch_pdl may start while
+// the previous kernel on the stream finishes its last blocks; it calls pdl_wait()
+// before touching any memory, which returns once that kernel has completed and its
+// writes are visible.  (Without the launch attribute pdl_wait returns at once.)
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 
 // Matches the WF_DTYPE_* constants of include/wayfinder.h.
 enum Dtype : int { kBF16 = 0, kF16 = 1, kF32 = 2 };

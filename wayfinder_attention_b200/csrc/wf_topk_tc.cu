@@ -746,6 +746,7 @@ __device__ __forceinline__ void finalize_row(const FinParams& p, int64_t row, co
 
 template <int SE, int KB>
 __global__ void __launch_bounds__(kFinWarps * 32, 2) topk_finalize_kernel(const FinParams p) {
+  pdl_wait();
   __shared__ uint32_t skey[kFinWarps][KB];
   __shared__ int sidx[kFinWarps][KB];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -765,6 +766,7 @@ __global__ void __launch_bounds__(kFinWarps * 32, 2) topk_finalize_kernel(const 
 // Rows whose lists hold K candidates or fewer need no selection and are skipped.
 template <typename TI, int R, bool F32>
 __global__ void __launch_bounds__(256) topk_rescore_kernel(const FinParams p) {
+  pdl_wait();
   const int64_t wl = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);  // (row, list)
   const int lane = threadIdx.x & 31;
   if (wl >= (int64_t)p.B * p.Tq * kLists) return;
@@ -985,8 +987,10 @@ int launch_t(const TopkParams& p, cudaStream_t stream) {
     f.lim = t.lim;
     f.src = t.src;
     const size_t rows = (size_t)nb * p.Tq;
-    topk_rescore_kernel<TI, R, F32><<<(unsigned)((rows * kLists + 7) / 8), 256, 0, stream>>>(f);
-    topk_finalize_kernel<SE, KW - 128><<<(unsigned)((rows + kFinWarps - 1) / kFinWarps), kFinWarps * 32, 0, stream>>>(f);
+    e = launch_pdl(topk_rescore_kernel<TI, R, F32>, dim3((unsigned)((rows * kLists + 7) / 8)), dim3(256), 0, stream, f);
+    if (e != cudaSuccess) return (int)e;
+    e = launch_pdl(topk_finalize_kernel<SE, KW - 128>, dim3((unsigned)((rows + kFinWarps - 1) / kFinWarps)),
+                   dim3(kFinWarps * 32), 0, stream, f);
     e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
   }
